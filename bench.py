@@ -1,0 +1,379 @@
+"""GSA forward benchmark on B200: tokens/s of GatedSparseAttention.forward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3] [--impl ours|reference]
+
+One step = one forward of the configuration's whole batch (default cfg3:
+B=1, T=16384, D=2048, H=16, k=2048, bf16) on synthetic seeded inputs and
+weights.  For N > 1 the driver launches one rank per GPU under torchrun; B=1
+configurations shard query rows zig-zag over the ranks (k_I/K/V and the output
+rows are all-gathered with NCCL), batched ones shard sequences.
+
+Rank 0 prints ONE JSON line.  ``value`` is whole-job tokens/s with inputs
+resident in HBM, timed per step with CUDA events (max over ranks), L2 flushed
+between steps outside the timed events; ``e2e`` repeats the measurement
+through the public module API from pinned host memory with the host->device
+copy of x and the device->host read of the output inside the timed region.
+``roofline`` describes the dominant kernel (the tensor-core sparse attention),
+timed live with events on its launch stream; ``cpu_baseline`` times the CPU
+oracle (a restatement of gsa_ref.py) on a bounded row sample on this host.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle port of
+gsa_ref.py; the reference itself is Python and does not travel) on all host
+cores for the same workload and prints the same JSON line with impl=reference.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "GSA fwd tokens/s at D=2048,T=16K (1-8 B200); indexer TFLOP/s, sparse-attn GB/s"
+UNIT = "tokens/s"
+# dram__bytes_read.sum + dram__bytes_write.sum of one masked-attention launch
+# from the ncu capture summarised in profiles/ (None until captured).
+ATTN_TRAFFIC_BYTES_PER_LAUNCH = None
+ATTN_TRAFFIC_NOTE = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg3")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-rows", type=int, default=256)
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["_source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "_source": "fallback"}
+
+
+# ─────────────────────────────────────────────────────────────── clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except ValueError:
+                continue
+        try:
+            os.unlink(self.file.name)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ─────────────────────────────────────────────────────────────── CPU baseline
+def cpu_baseline(cfg, sample_rows: int, threads: int) -> dict:
+    """Time the CPU oracle (restated gsa_ref.py) on a bounded row sample.
+
+    Work shared by all rows (key/value/indexer-key projections + key RoPE over
+    the full sequence) is timed once; the per-row work is timed on
+    ``sample_rows`` query rows spread uniformly over T and scaled by T/S."""
+    from gsa_gdn_benchmarkstudy_b200.gsa import GatedSparseAttention
+    from gsa_gdn_benchmarkstudy_b200.workloads import init_weights_, make_input
+    from oracle import gsa_oracle as O
+
+    torch.set_num_threads(threads)
+    m = GatedSparseAttention(**cfg.module_kwargs())
+    init_weights_(m, seed=1)
+    sd = m.to(cfg.torch_dtype).state_dict()
+    x = make_input(cfg)
+    total_s = 0.0
+    rows_desc = []
+    with torch.no_grad():
+        for b in range(cfg.B):
+            rows = O.spread_rows(cfg.T, sample_rows, offset=b)
+            tm: dict = {}
+            O.forward_rows(sd, x[b:b + 1], cfg.H, cfg.k_base, cfg.k_max, rows=rows,
+                           row_chunk=1, timings=tm)
+            total_s += tm["shared_s"] + tm["rows_s"] * cfg.T / len(rows)
+            rows_desc.append(len(rows))
+            if b == 0 and cfg.B > 1:
+                # sequences of a batch cost the same: extrapolate from the first
+                total_s *= cfg.B
+                break
+    return {"value": cfg.B * cfg.T / total_s, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"{rows_desc[0]} query rows spread over T={cfg.T} of sequence 0 "
+                       f"(+ full-sequence key/value projections), per-row time scaled by "
+                       f"T/rows{' and by B' if cfg.B > 1 else ''}; oracle restatement of "
+                       f"gsa_ref.py in torch on the CPU, {cfg.dtype}")}
+
+
+# ─────────────────────────────────────────────────────────────── reference arm
+def run_reference(args, cfg, rank: int):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    sample = max(8, min(args.cpu_sample_rows, 64))
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(cfg, sample, threads)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cfg.B * cfg.T / v * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": cfg.dtype, "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights)",
+        "config": {"workload": f"{cfg.name}: B={cfg.B} T={cfg.T} D={cfg.D} H={cfg.H} "
+                               f"k={cfg.k_eff}", "l2": "n/a (CPU)"},
+        "cpu_baseline": {**r, "value": v},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ─────────────────────────────────────────────────────────────── our arm
+def build_model(cfg, device):
+    from gsa_gdn_benchmarkstudy_b200 import GatedSparseAttention
+    from gsa_gdn_benchmarkstudy_b200.workloads import init_weights_
+
+    m = GatedSparseAttention(**cfg.module_kwargs())
+    init_weights_(m, seed=1)
+    m = m.to(cfg.torch_dtype).to(device).eval()
+    m.fuse_projections()
+    return m
+
+
+def run_ours(args, cfg, rank: int, world: int, device):
+    from gsa_gdn_benchmarkstudy_b200 import _lib
+    from gsa_gdn_benchmarkstudy_b200.build import build
+    from gsa_gdn_benchmarkstudy_b200.workloads import WorkModel, make_input
+
+    if rank == 0:
+        build()
+    if world > 1:
+        dist.barrier()
+    _lib.load()
+    torch.set_grad_enabled(False)
+    model = build_model(cfg, device)
+    x_host = make_input(cfg).pin_memory()
+
+    if world > 1:
+        from gsa_gdn_benchmarkstudy_b200.sharding import ShardedGSA
+        runner = ShardedGSA(model, dist.group.WORLD, T=cfg.T, B=cfg.B)
+        x_dev = runner.local_input(x_host.to(device))
+        step = lambda: runner(x_dev)  # noqa: E731
+        e2e_step = lambda xh: runner.forward_host(xh)  # noqa: E731
+    else:
+        x_dev = x_host.to(device)
+        step = lambda: model(x_dev)  # noqa: E731
+        e2e_step = None
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)  # > 126 MB L2
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---------------- device-resident timed region (K steps, per-step events)
+    model._stage_events = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index if device.index is not None else 0) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    stage_events = model._stage_events
+    model._stage_events = None
+    local_ms = sum(step_ms)
+    t = torch.tensor([local_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = t.item()
+    ms_per_step = total_ms / args.steps
+    value = cfg.B * cfg.T / (ms_per_step / 1e3)
+
+    # per-kernel averages over the timed region (events on the launch stream)
+    stage_ms: dict = {}
+    for name, a, b in stage_events:
+        stage_ms.setdefault(name, []).append(a.elapsed_time(b))
+    stage_avg = {k: sum(v) / len(v) for k, v in stage_ms.items()}
+    launches_per_step = sum(len(v) for k, v in stage_ms.items() if k.startswith("k:")) / args.steps
+
+    # ---------------- end-to-end through the public API, host buffers
+    out_host = torch.empty(cfg.B, cfg.T, cfg.D, dtype=cfg.torch_dtype).pin_memory()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        e2e_ev[i][0].record(stream)
+        if e2e_step is None:
+            xd = x_host.to(device, non_blocking=True)
+            out = model(xd)
+            out_host.copy_(out, non_blocking=True)
+        else:
+            e2e_step(x_host)
+        e2e_ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_local = sum(a.elapsed_time(b) for a, b in e2e_ev)
+    t = torch.tensor([e2e_local], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = t.item() / args.steps
+    h2d = x_host.numel() * x_host.element_size() // (world if world > 1 else 1) * (world if world > 1 else 1)
+    d2h = out_host.numel() * out_host.element_size()
+
+    if rank != 0:
+        return
+    pk = peaks()
+    wm = WorkModel(cfg)
+    attn_ms = stage_avg.get("k:masked_attention")
+    idx_ms = stage_avg.get("k:indexer")
+    rl = None
+    if attn_ms:
+        # algorithmic work of one launch: QK^T + PV over the causal key range of the
+        # launch's rows (the formulation the kernel computes), B sequences / world ranks
+        flops = wm.attn_dense_flops / world / stage_count(stage_ms, "k:masked_attention", args.steps)
+        achieved = flops / (attn_ms / 1e3) / 1e12
+        peak = pk["bf16_tflops"]
+        rl = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+              "frac": round(achieved / peak, 4), "traffic": ATTN_TRAFFIC_BYTES_PER_LAUNCH,
+              "kernel": "masked_attn_kernel (tcgen05)", "peak_kind": f"bf16 burst, {pk['_source']}",
+              "ms_per_launch": round(attn_ms, 4)}
+        if ATTN_TRAFFIC_NOTE:
+            rl["traffic_note"] = ATTN_TRAFFIC_NOTE
+    extra = {}
+    if idx_ms:
+        n_idx = stage_count(stage_ms, "k:indexer", args.steps)
+        extra["indexer_tflops"] = round(wm.indexer_flops / world / n_idx / (idx_ms / 1e3) / 1e12, 2)
+    if attn_ms:
+        n_at = stage_count(stage_ms, "k:masked_attention", args.steps)
+        extra["sparse_attn_gather_equiv_gbs"] = round(
+            wm.attn_gather_bytes / world / n_at / (attn_ms / 1e3) / 1e9, 1)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16"
+        if cfg.dtype == "bf16" else "f32",
+        "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights; no dataset in the reference)",
+        "config": {"workload": f"{cfg.name}: B={cfg.B} T={cfg.T} D={cfg.D} H={cfg.H} d=128 "
+                               f"H_I=4 d_I=64 k={cfg.k_eff}",
+                   "global_batch": cfg.B, "seq_len": cfg.T,
+                   "parallelism": ("single GPU" if world == 1 else
+                                   ("query-row zig-zag shards" if cfg.B == 1 else "batch shards")),
+                   "l2": "flushed between steps (256 MB memset outside the step events)"},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": clocks.summary(),
+        "e2e": {"value": round(cfg.B * cfg.T / (e2e_ms / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "ms_per_step": round(e2e_ms, 4)},
+        "roofline": rl,
+        "stage_ms": {k[2:]: round(v, 4) for k, v in stage_avg.items()},
+        **extra,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_sample_rows, os.cpu_count() or 1)
+    print(json.dumps(line), flush=True)
+
+
+def stage_count(stage_ms: dict, name: str, steps: int) -> float:
+    return len(stage_ms.get(name, [])) / steps
+
+
+def main():
+    args = parse_args()
+    from gsa_gdn_benchmarkstudy_b200.workloads import CONFIGS
+
+    cfg = CONFIGS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    try:
+        run_ours(args, cfg, rank, world, device)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

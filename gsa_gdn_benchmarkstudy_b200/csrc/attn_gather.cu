@@ -1,0 +1,167 @@
+// attn_gather.cu — index-gather sparse attention for explicit (indices, mask)
+// inputs, fp32 online softmax.
+//
+// Reference: _gather_along_seq + sparse_attention_ref (gsa_ref.py:185-238)
+// and the Triton _fused_sparse_attn_kernel (gsa_opt.py:199-346): for every
+// (b, t, h), softmax over the selected slots of (q . K[idx] * scale), times
+// V[idx]; indices clamped to [0, Tkv-1] (gsa_ref.py:196); masked slots take
+// no part; a row whose slots are all masked yields zeros (nan_to_num at
+// gsa_ref.py:235).  Unlike the Triton kernel, masked slots are skipped
+// without loading their K/V rows, and duplicate indices count once per slot
+// exactly as in the reference.
+//
+// One warp per (b, t, h): every lane owns d/32 consecutive channels; each
+// warp reads 32 (index, mask) pairs with one coalesced load and broadcasts
+// them by shuffle; K and V rows are read with vector loads.
+#include "kernels.h"
+
+namespace gsa {
+namespace {
+
+template <typename E, int D>
+struct Lanes;
+
+template <int D>
+struct Lanes<__nv_bfloat16, D> {
+  static constexpr int N = D / 32;  // channels per lane (2, 4 or 8)
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&x)[N]) {
+    if constexpr (N == 8) {
+      uint4 raw = *reinterpret_cast<const uint4*>(p);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(e[i]);
+    } else if constexpr (N == 4) {
+      uint2 raw = *reinterpret_cast<const uint2*>(p);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(e[i]);
+    } else {
+      uint32_t raw = *reinterpret_cast<const uint32_t*>(p);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      x[0] = __bfloat162float(e[0]);
+      x[1] = __bfloat162float(e[1]);
+    }
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float (&x)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2)
+      *reinterpret_cast<uint32_t*>(p + i) = pack_bf16x2(x[i], x[i + 1]);
+  }
+};
+
+template <int D>
+struct Lanes<float, D> {
+  static constexpr int N = D / 32;
+  static __device__ __forceinline__ void load(const float* p, float (&x)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+      const float2 v = *reinterpret_cast<const float2*>(p + i);
+      x[i] = v.x;
+      x[i + 1] = v.y;
+    }
+  }
+  static __device__ __forceinline__ void store(float* p, const float (&x)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) *reinterpret_cast<float2*>(p + i) = make_float2(x[i], x[i + 1]);
+  }
+};
+
+template <typename E, int D>
+__global__ void __launch_bounds__(256) gather_attn_kernel(
+    const E* __restrict__ q, int64_t q_stride, const E* __restrict__ k, int64_t k_stride,
+    const E* __restrict__ v, int64_t v_stride, const int32_t* __restrict__ indices,
+    const uint8_t* __restrict__ mask, int k_sel, E* __restrict__ out, int64_t out_stride,
+    float scale, int B, int Tq, int Tkv, int H) {
+  using L = Lanes<E, D>;
+  constexpr int N = L::N;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= static_cast<int64_t>(B) * Tq * H) return;
+  const int h = static_cast<int>(gw % H);
+  const int64_t row = gw / H;  // b * Tq + t
+  const int b = static_cast<int>(row / Tq);
+  const int ch = h * D + lane * N;
+
+  float qv[N];
+  L::load(q + row * q_stride + ch, qv);
+  float m = -INFINITY, l = 0.f, acc[N];
+#pragma unroll
+  for (int e = 0; e < N; ++e) acc[e] = 0.f;
+
+  const int32_t* irow = indices + row * k_sel;
+  const uint8_t* mrow = mask ? mask + row * k_sel : nullptr;
+  const E* kb = k + static_cast<int64_t>(b) * Tkv * k_stride + ch;
+  const E* vb = v + static_cast<int64_t>(b) * Tkv * v_stride + ch;
+
+  for (int s0 = 0; s0 < k_sel; s0 += 32) {
+    const int s = s0 + lane;
+    int jl = 0;
+    bool vl = false;
+    if (s < k_sel) {
+      jl = min(max(irow[s], 0), Tkv - 1);
+      vl = mrow ? (mrow[s] != 0) : true;
+    }
+    uint32_t live = __ballot_sync(0xFFFFFFFFu, vl);
+    while (live) {
+      const int src = __ffs(live) - 1;
+      live &= live - 1;
+      const int j = __shfl_sync(0xFFFFFFFFu, jl, src);
+      float kv[N], vv[N];
+      L::load(kb + static_cast<int64_t>(j) * k_stride, kv);
+      L::load(vb + static_cast<int64_t>(j) * v_stride, vv);
+      float part = 0.f;
+#pragma unroll
+      for (int e = 0; e < N; ++e) part = fmaf(qv[e], kv[e], part);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
+      const float sc = part * scale;
+      const float m_new = fmaxf(m, sc);
+      const float alpha = expf(m - m_new);  // 0 on the first live slot (m = -inf)
+      const float p = expf(sc - m_new);
+      l = l * alpha + p;
+#pragma unroll
+      for (int e = 0; e < N; ++e) acc[e] = fmaf(p, vv[e], acc[e] * alpha);
+      m = m_new;
+    }
+  }
+  const float inv = l > 0.f ? 1.0f / l : 0.f;
+#pragma unroll
+  for (int e = 0; e < N; ++e) acc[e] *= inv;
+  L::store(out + row * out_stride + ch, acc);
+}
+
+template <typename E>
+cudaError_t launch_typed(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                         const void* v, int64_t v_stride, const int32_t* indices,
+                         const uint8_t* mask, int k_sel, void* out, int64_t out_stride,
+                         float scale, int B, int Tq, int Tkv, int H, int d, cudaStream_t stream) {
+  const int64_t warps = static_cast<int64_t>(B) * Tq * H;
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+#define GSA_GATHER_CASE(DD)                                                                    \
+  gather_attn_kernel<E, DD><<<blocks, 256, 0, stream>>>(                                       \
+      static_cast<const E*>(q), q_stride, static_cast<const E*>(k), k_stride,                  \
+      static_cast<const E*>(v), v_stride, indices, mask, k_sel, static_cast<E*>(out),          \
+      out_stride, scale, B, Tq, Tkv, H)
+  if (d == 64) GSA_GATHER_CASE(64);
+  else if (d == 128) GSA_GATHER_CASE(128);
+  else GSA_GATHER_CASE(256);
+#undef GSA_GATHER_CASE
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gather_attention(const void* q, int64_t q_stride, const void* k,
+                                    int64_t k_stride, const void* v, int64_t v_stride,
+                                    const int32_t* indices, const uint8_t* mask, int k_sel,
+                                    void* out, int64_t out_stride, float scale, int dtype, int B,
+                                    int Tq, int Tkv, int H, int d, cudaStream_t stream) {
+  if (B == 0 || Tq == 0 || H == 0) return cudaSuccess;
+  if (dtype == GSA_DTYPE_BF16)
+    return launch_typed<__nv_bfloat16>(q, q_stride, k, k_stride, v, v_stride, indices, mask,
+                                       k_sel, out, out_stride, scale, B, Tq, Tkv, H, d, stream);
+  return launch_typed<float>(q, q_stride, k, k_stride, v, v_stride, indices, mask, k_sel, out,
+                             out_stride, scale, B, Tq, Tkv, H, d, stream);
+}
+
+}  // namespace gsa

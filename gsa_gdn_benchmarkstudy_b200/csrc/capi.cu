@@ -1,0 +1,350 @@
+// capi.cu — the extern "C" entry points of include/gsa_b200.h: argument
+// checks, TMA tensor-map construction, dispatch to the kernels, status codes.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "kernels.h"
+
+namespace {
+
+constexpr int kVersion = 10000;  // 1.0.0
+constexpr int kMaxDevices = 64;
+
+thread_local char g_last_error[256] = "";
+
+// Device word that kernels set when a bounded wait expires.
+__device__ int g_dev_err;
+
+int set_cuda_error(cudaError_t e) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return GSA_ERR_CUDA;
+}
+
+int set_error(int code, const char* what) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s", what);
+  return code;
+}
+
+// Per-device state: sm_100 check result and the address of g_dev_err.
+struct DeviceState {
+  bool ready = false;
+  bool sm100 = false;
+  int* err = nullptr;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  if (dev < 0 || dev >= kMaxDevices) return set_error(GSA_ERR_NO_DEVICE, "device index out of range");
+  DeviceState& st = g_dev[dev];
+  if (!st.ready) {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    if (!st.ready) {
+      int major = 0;
+      e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+      if (e != cudaSuccess) return set_cuda_error(e);
+      st.sm100 = (major == 10);
+      if (st.sm100) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_dev_err);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        st.err = static_cast<int*>(p);
+      }
+      st.ready = true;
+    }
+  }
+  if (!st.sm100) return set_error(GSA_ERR_NO_DEVICE, "current device is not sm_100 (B200)");
+  *out = &st;
+  return GSA_OK;
+}
+
+// ---------------------------------------------------------------- TMA maps
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                      const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                      CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled_t encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+  });
+  return fn;
+}
+
+// 3-D bf16 map over [z][y][x] with row stride `row_bytes` and batch stride
+// `batch_bytes`; box {64, box_y, 1} with 128-byte swizzle; zero fill out of
+// bounds.
+int make_map_bf16_3d(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z,
+                     uint64_t row_bytes, uint64_t batch_bytes, uint32_t box_y) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (!fn) return set_error(GSA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {x, y, z};
+  const cuuint64_t strides[2] = {row_bytes, batch_bytes};
+  const cuuint32_t box[3] = {64, box_y, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled failed (%d)",
+                  static_cast<int>(r));
+    return GSA_ERR_CUDA;
+  }
+  return GSA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int finish(cudaError_t e) { return e == cudaSuccess ? GSA_OK : set_cuda_error(e); }
+
+}  // namespace
+
+extern "C" {
+
+int gsa_version(void) { return kVersion; }
+
+const char* gsa_status_string(int status) {
+  switch (status) {
+    case GSA_OK: return "ok";
+    case GSA_ERR_INVALID_ARG: return "invalid argument";
+    case GSA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case GSA_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case GSA_ERR_CUDA: return "CUDA error";
+    case GSA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case GSA_ERR_NO_DEVICE: return "no usable sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+const char* gsa_last_error_string(void) { return g_last_error; }
+
+int gsa_device_error(int* out, int reset) {
+  if (!out) return set_error(GSA_ERR_INVALID_ARG, "out is NULL");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_cuda_error(e);
+  e = cudaMemcpy(out, st->err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  if (reset) {
+    e = cudaMemset(st->err, 0, sizeof(int));
+    if (e != cudaSuccess) return set_cuda_error(e);
+  }
+  return GSA_OK;
+}
+
+int64_t gsa_bitmask_words(int Tkv) {
+  if (Tkv <= 0) return 0;
+  return 4 * ((static_cast<int64_t>(Tkv) + 127) / 128);
+}
+
+int gsa_rope_gates(const void* q_src, const void* k_src, const void* v_src, const void* vg_src,
+                   int64_t src_stride, int dtype, int B, int T, int H, int d, const void* cos,
+                   const void* sin, void* q_out, void* k_out, void* v_out, void* stream) {
+  if (dtype != GSA_DTYPE_BF16 && dtype != GSA_DTYPE_F32)
+    return set_error(GSA_ERR_UNSUPPORTED, "dtype must be bf16 or f32");
+  if (B < 0 || T < 0 || H <= 0 || d <= 0) return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (d % 16 != 0) return set_error(GSA_ERR_UNSUPPORTED, "d must be a multiple of 16");
+  if (B == 0 || T == 0) return GSA_OK;
+  if (!q_src || !k_src || !cos || !sin || !q_out || !k_out)
+    return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  if ((v_src == nullptr) != (vg_src == nullptr) || (v_src && !v_out))
+    return set_error(GSA_ERR_INVALID_ARG, "v_src, vg_src and v_out go together");
+  const int es = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  const int64_t width = static_cast<int64_t>(H) * d;
+  if (src_stride < width) return set_error(GSA_ERR_INVALID_ARG, "src_stride < H*d");
+  if ((src_stride * es) % 16 || !aligned16(q_src) || !aligned16(k_src) ||
+      (v_src && (!aligned16(v_src) || !aligned16(vg_src) || !aligned16(v_out))) ||
+      !aligned16(cos) || !aligned16(sin) || !aligned16(q_out) || !aligned16(k_out))
+    return set_error(GSA_ERR_ALIGNMENT, "rows must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  return finish(gsa::launch_rope_gates(q_src, k_src, v_src, vg_src, src_stride, dtype, B, T, H, d,
+                                       cos, sin, q_out, k_out, v_out,
+                                       static_cast<cudaStream_t>(stream)));
+}
+
+int gsa_indexer_scores(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                       const void* w, int64_t w_stride, const float* bias, float scale, int dtype,
+                       int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I, float* out,
+                       int64_t out_stride, int fill_upper, void* stream) {
+  if (dtype != GSA_DTYPE_BF16 && dtype != GSA_DTYPE_F32)
+    return set_error(GSA_ERR_UNSUPPORTED, "dtype must be bf16 or f32");
+  if (B < 0 || Tq < 0 || Tkv < 0 || q_pos0 < 0 || H_I <= 0 || d_I <= 0)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (B == 0 || Tq == 0 || Tkv == 0) return GSA_OK;
+  if (!q || !k || !w || !bias || !out) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  if (out_stride < Tkv) return set_error(GSA_ERR_INVALID_ARG, "out_stride < Tkv");
+  if (q_stride < static_cast<int64_t>(H_I) * d_I || k_stride < d_I || w_stride < H_I)
+    return set_error(GSA_ERR_INVALID_ARG, "row stride smaller than the row");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fill_upper) {
+    cudaError_t e = gsa::launch_fill_upper(out, out_stride, B, Tq, Tkv, q_pos0, s);
+    if (e != cudaSuccess) return set_cuda_error(e);
+  }
+  if (dtype == GSA_DTYPE_BF16 && H_I == 4 && d_I == 64) {
+    if (!aligned16(q) || !aligned16(k) || (q_stride * 2) % 16 || (k_stride * 2) % 16 ||
+        !aligned16(out) || (out_stride * 4) % 16)
+      return set_error(GSA_ERR_ALIGNMENT, "indexer rows must be 16-byte aligned");
+    CUtensorMap qmap, kmap;
+    rc = make_map_bf16_3d(&qmap, q, static_cast<uint64_t>(H_I) * d_I, Tq, B, q_stride * 2,
+                          static_cast<uint64_t>(Tq) * q_stride * 2, 128);
+    if (rc) return rc;
+    rc = make_map_bf16_3d(&kmap, k, d_I, Tkv, B, k_stride * 2,
+                          static_cast<uint64_t>(Tkv) * k_stride * 2, 32);
+    if (rc) return rc;
+    gsa::IndexerArgs a;
+    a.w = w;
+    a.w_stride = w_stride;
+    a.bias = bias;
+    a.scale = scale;
+    a.B = B;
+    a.Tq = Tq;
+    a.Tkv = Tkv;
+    a.q_pos0 = q_pos0;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.err = st->err;
+    return finish(gsa::launch_indexer_tc(qmap, kmap, a, s));
+  }
+  if (H_I > 8 || d_I > 128 || H_I * d_I > 512)
+    return set_error(GSA_ERR_UNSUPPORTED, "indexer heads/dims beyond the CUDA-core kernel");
+  return finish(gsa::launch_indexer_simt(q, q_stride, k, k_stride, w, w_stride, bias, scale,
+                                         dtype, B, Tq, Tkv, q_pos0, H_I, d_I, out, out_stride,
+                                         s));
+}
+
+int gsa_topk_select(const float* scores, int64_t score_stride, int B, int Tq, int Tkv, int q_pos0,
+                    int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                    int64_t bitmask_words, void* stream) {
+  if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0 || k_sel <= 0 || k_sel > Tkv)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes (need 0 < k_sel <= Tkv)");
+  if (B == 0 || Tq == 0) return GSA_OK;
+  if (!scores) return set_error(GSA_ERR_INVALID_ARG, "scores is NULL");
+  if (score_stride < Tkv) return set_error(GSA_ERR_INVALID_ARG, "score_stride < Tkv");
+  if (bitmask && bitmask_words < gsa_bitmask_words(Tkv))
+    return set_error(GSA_ERR_INVALID_ARG, "bitmask_words < gsa_bitmask_words(Tkv)");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  return finish(gsa::launch_topk(scores, score_stride, B, Tq, Tkv, q_pos0, k_sel, indices, mask,
+                                 bitmask, bitmask_words, static_cast<cudaStream_t>(stream)));
+}
+
+int gsa_masked_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                         const void* v, int64_t v_stride, const uint32_t* bitmask,
+                         int64_t bitmask_words, const void* og, int64_t og_stride, void* out,
+                         int64_t out_stride, float scale, int B, int Tq, int Tkv, int q_pos0,
+                         int H, int d, void* stream) {
+  if (B < 0 || Tq < 0 || Tkv < 0 || q_pos0 < 0 || H <= 0 || d <= 0)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (d != 128) return set_error(GSA_ERR_UNSUPPORTED, "masked attention needs d == 128");
+  if (B == 0 || Tq == 0 || Tkv == 0) return GSA_OK;
+  if (!q || !k || !v || !bitmask || !out) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  const int64_t width = static_cast<int64_t>(H) * d;
+  if (q_stride < width || k_stride < width || v_stride < width || out_stride < width ||
+      (og && og_stride < width))
+    return set_error(GSA_ERR_INVALID_ARG, "row stride smaller than H*d");
+  if (bitmask_words < gsa_bitmask_words(Tkv) || bitmask_words % 4)
+    return set_error(GSA_ERR_INVALID_ARG, "bitmask_words must be >= gsa_bitmask_words(Tkv), %4");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(bitmask) ||
+      (og && !aligned16(og)) || (q_stride * 2) % 16 || (k_stride * 2) % 16 ||
+      (v_stride * 2) % 16 || (out_stride * 2) % 16 || (og && (og_stride * 2) % 16))
+    return set_error(GSA_ERR_ALIGNMENT, "attention rows must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  CUtensorMap qmap, kmap, vmap;
+  rc = make_map_bf16_3d(&qmap, q, width, Tq, B, q_stride * 2,
+                        static_cast<uint64_t>(Tq) * q_stride * 2, 128);
+  if (rc) return rc;
+  rc = make_map_bf16_3d(&kmap, k, width, Tkv, B, k_stride * 2,
+                        static_cast<uint64_t>(Tkv) * k_stride * 2, 128);
+  if (rc) return rc;
+  rc = make_map_bf16_3d(&vmap, v, width, Tkv, B, v_stride * 2,
+                        static_cast<uint64_t>(Tkv) * v_stride * 2, 128);
+  if (rc) return rc;
+  gsa::MaskedAttnArgs a;
+  a.bitmask = bitmask;
+  a.bitmask_words = bitmask_words;
+  a.og = og;
+  a.og_stride = og_stride;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.scale = scale;
+  a.B = B;
+  a.Tq = Tq;
+  a.Tkv = Tkv;
+  a.q_pos0 = q_pos0;
+  a.H = H;
+  a.err = st->err;
+  return finish(gsa::launch_masked_attention(qmap, kmap, vmap, a, static_cast<cudaStream_t>(stream)));
+}
+
+int gsa_gather_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                         const void* v, int64_t v_stride, const int32_t* indices,
+                         const uint8_t* mask, int k_sel, void* out, int64_t out_stride,
+                         float scale, int dtype, int B, int Tq, int Tkv, int H, int d,
+                         void* stream) {
+  if (dtype != GSA_DTYPE_BF16 && dtype != GSA_DTYPE_F32)
+    return set_error(GSA_ERR_UNSUPPORTED, "dtype must be bf16 or f32");
+  if (B < 0 || Tq < 0 || Tkv <= 0 || H <= 0 || k_sel < 0)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (d != 64 && d != 128 && d != 256) return set_error(GSA_ERR_UNSUPPORTED, "d must be 64/128/256");
+  if (B == 0 || Tq == 0) return GSA_OK;
+  if (!q || !k || !v || !out || (k_sel > 0 && !indices))
+    return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  const int64_t width = static_cast<int64_t>(H) * d;
+  if (q_stride < width || k_stride < width || v_stride < width || out_stride < width)
+    return set_error(GSA_ERR_INVALID_ARG, "row stride smaller than H*d");
+  const int es = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      (q_stride * es) % 16 || (k_stride * es) % 16 || (v_stride * es) % 16 ||
+      (out_stride * es) % 16)
+    return set_error(GSA_ERR_ALIGNMENT, "attention rows must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  return finish(gsa::launch_gather_attention(q, q_stride, k, k_stride, v, v_stride, indices, mask,
+                                             k_sel, out, out_stride, scale, dtype, B, Tq, Tkv, H,
+                                             d, static_cast<cudaStream_t>(stream)));
+}
+
+int gsa_output_gate(const void* o, int64_t o_stride, const void* og, int64_t og_stride, void* out,
+                    int64_t out_stride, int dtype, int rows, int width, void* stream) {
+  if (dtype != GSA_DTYPE_BF16 && dtype != GSA_DTYPE_F32)
+    return set_error(GSA_ERR_UNSUPPORTED, "dtype must be bf16 or f32");
+  if (rows < 0 || width < 0) return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (width % 8) return set_error(GSA_ERR_UNSUPPORTED, "width must be a multiple of 8");
+  if (rows == 0 || width == 0) return GSA_OK;
+  if (!o || !og || !out) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  const int es = dtype == GSA_DTYPE_BF16 ? 2 : 4;
+  if (!aligned16(o) || !aligned16(og) || !aligned16(out) || (o_stride * es) % 16 ||
+      (og_stride * es) % 16 || (out_stride * es) % 16)
+    return set_error(GSA_ERR_ALIGNMENT, "rows must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  return finish(gsa::launch_output_gate(o, o_stride, og, og_stride, out, out_stride, dtype, rows,
+                                        width, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

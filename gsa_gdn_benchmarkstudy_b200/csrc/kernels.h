@@ -1,0 +1,68 @@
+// kernels.h — internal launchers behind the C ABI (include/gsa_b200.h).
+// Argument checking happens in capi.cu; these assume valid arguments.
+#pragma once
+
+#include "common.cuh"
+
+namespace gsa {
+
+cudaError_t launch_rope_gates(const void* q_src, const void* k_src, const void* v_src,
+                              const void* vg_src, int64_t src_stride, int dtype, int B, int T,
+                              int H, int d, const void* cos_t, const void* sin_t, void* q_out,
+                              void* k_out, void* v_out, cudaStream_t stream);
+
+cudaError_t launch_output_gate(const void* o, int64_t o_stride, const void* og, int64_t og_stride,
+                               void* out, int64_t out_stride, int dtype, int rows, int width,
+                               cudaStream_t stream);
+
+// Tensor-core indexer (bf16, H_I = 4, d_I = 64).  Tensor maps are built by
+// the caller (capi.cu).
+struct IndexerArgs {
+  const void* w;
+  int64_t w_stride;
+  const float* bias;
+  float scale;
+  int B, Tq, Tkv, q_pos0;
+  float* out;
+  int64_t out_stride;
+  int* err;
+};
+cudaError_t launch_indexer_tc(const CUtensorMap& qmap, const CUtensorMap& kmap,
+                              const IndexerArgs& a, cudaStream_t stream);
+
+// CUDA-core indexer (fp32 or bf16 inputs, any H_I <= 8, d_I <= 128).
+cudaError_t launch_indexer_simt(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                                const void* w, int64_t w_stride, const float* bias, float scale,
+                                int dtype, int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                                float* out, int64_t out_stride, cudaStream_t stream);
+
+// Writes -inf into out[b, r, j] for q_pos0 + r < j < Tkv.
+cudaError_t launch_fill_upper(float* out, int64_t out_stride, int B, int Tq, int Tkv, int q_pos0,
+                              cudaStream_t stream);
+
+cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                        int q_pos0, int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                        int64_t bitmask_words, cudaStream_t stream);
+
+struct MaskedAttnArgs {
+  const uint32_t* bitmask;
+  int64_t bitmask_words;
+  const void* og;
+  int64_t og_stride;
+  void* out;
+  int64_t out_stride;
+  float scale;
+  int B, Tq, Tkv, q_pos0, H;
+  int* err;
+};
+cudaError_t launch_masked_attention(const CUtensorMap& qmap, const CUtensorMap& kmap,
+                                    const CUtensorMap& vmap, const MaskedAttnArgs& a,
+                                    cudaStream_t stream);
+
+cudaError_t launch_gather_attention(const void* q, int64_t q_stride, const void* k,
+                                    int64_t k_stride, const void* v, int64_t v_stride,
+                                    const int32_t* indices, const uint8_t* mask, int k_sel,
+                                    void* out, int64_t out_stride, float scale, int dtype, int B,
+                                    int Tq, int Tkv, int H, int d, cudaStream_t stream);
+
+}  // namespace gsa

@@ -1,0 +1,354 @@
+"""GatedSparseAttention for B200: the reference module's interface over sm_100a kernels.
+
+Drop-in for ``gsa_triton/gsa_ref.py::GatedSparseAttention`` (gsa_ref.py:243-325)
+and ``gsa_triton/gsa_opt.py::GatedSparseAttention`` (gsa_opt.py:512-730):
+same constructor arguments, sub-module names and ``state_dict`` keys,
+``forward(x, attention_mask=None)`` (the mask is accepted and ignored, as in
+the reference) and ``fuse_projections()``.
+
+Forward pipeline (bf16):
+  1. one cuBLAS GEMM over the fused, zero-padded weight
+     [q | k | v | value_gate | output_gate | idx_q | idx_k | idx_w | pad]
+     (the reference's separate projections, gsa_ref.py:283-285,100-102,164,178);
+  2. ``gsa_rope_gates``: RoPE on q/k + v * sigmoid(value gate);
+  3. ``gsa_indexer_scores``: tcgen05 gated indexer over causal key tiles;
+  4. ``gsa_topk_select``: per-row top-k -> selection bitmask;
+  5. ``gsa_masked_attention``: tcgen05 attention over the selected keys with
+     the output gate fused into its epilogue;
+  6. o_proj on cuBLAS.
+fp32 modules use the same steps with the CUDA-core indexer and the
+index-gather attention kernel.  There is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+try:  # NVTX ranges per stage, no-ops without CUDA (gsa_ref.py:17-24)
+    from torch.cuda import nvtx as _nvtx
+
+    _nvtx_push = _nvtx.range_push
+    _nvtx_pop = _nvtx.range_pop
+except Exception:  # pragma: no cover
+    def _nvtx_push(msg: str) -> None:
+        pass
+
+    def _nvtx_pop() -> None:
+        pass
+
+
+class _Stage:
+    """NVTX range around one stage; with ``module._stage_events`` set to a list it
+    also records a CUDA event pair on the current stream (used by bench.py to
+    time each kernel inside the timed region)."""
+
+    __slots__ = ("mod", "name", "nvtx", "a")
+
+    def __init__(self, mod, name: str, nvtx: str):
+        self.mod, self.name, self.nvtx, self.a = mod, name, nvtx, None
+
+    def __enter__(self):
+        _nvtx_push(self.nvtx)
+        if self.mod._stage_events is not None:
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.a is not None:
+            b = torch.cuda.Event(enable_timing=True)
+            b.record()
+            self.mod._stage_events.append((self.name, self.a, b))
+        _nvtx_pop()
+        return False
+
+
+# ── Rotary embeddings ──────────────────────────────────────────────────────
+
+class RotaryEmbedding(nn.Module):
+    """Rotary table holder with the reference's buffers and cache semantics.
+
+    Mirrors gsa_ref.py:43-70: ``inv_freq`` is a persistent buffer (so it is
+    rounded to the module dtype by ``.to(dtype)``), ``cos_cached`` /
+    ``sin_cached`` are non-persistent and built for 8192 positions at
+    construction.  A longer sequence rebuilds the cache from the *current*
+    ``inv_freq`` in float32 on the host, exactly as the reference's
+    ``_set_cos_sin_cache`` does on CPU (on CUDA the reference's rebuild mixes
+    a CPU ``arange`` with a CUDA ``inv_freq`` and raises).  Tables are returned
+    in the requested dtype.
+    """
+
+    def __init__(self, dim: int, max_seq_len: int = 8192, base: float = 10000.0):
+        super().__init__()
+        self.dim = dim
+        inv_freq = 1.0 / (base ** (torch.arange(0, dim, 2).float() / dim))
+        self.register_buffer("inv_freq", inv_freq)
+        self._set_cos_sin_cache(max_seq_len)
+
+    def _set_cos_sin_cache(self, seq_len: int) -> None:
+        inv = self.inv_freq.detach().cpu()
+        t = torch.arange(seq_len, dtype=torch.float32)
+        freqs = torch.outer(t, inv)
+        emb = torch.cat((freqs, freqs), dim=-1)
+        self.register_buffer("cos_cached", emb.cos(), persistent=False)
+        self.register_buffer("sin_cached", emb.sin(), persistent=False)
+
+    def forward(self, seq_len: int, device: torch.device, dtype: torch.dtype = None
+                ) -> Tuple[torch.Tensor, torch.Tensor]:
+        if seq_len > self.cos_cached.shape[0]:
+            self._set_cos_sin_cache(seq_len)
+            self.cos_cached = self.cos_cached.to(device)
+            self.sin_cached = self.sin_cached.to(device)
+        cos = self.cos_cached[:seq_len].to(device)
+        sin = self.sin_cached[:seq_len].to(device)
+        if dtype is not None:
+            cos = cos.to(dtype)
+            sin = sin.to(dtype)
+        return cos, sin
+
+
+def apply_rotary_pos_emb(q, k, cos, sin):
+    """Reference signature (gsa_ref.py:35-40), computed by the CUDA RoPE kernel."""
+    return ops.apply_rotary_pos_emb(q, k, cos, sin)
+
+
+# ── Gated lightning indexer ────────────────────────────────────────────────
+
+class GatedLightningIndexer(nn.Module):
+    """score[q,k] = sum_h sigmoid(w[q,h]) * sigmoid(q_I[q,h].k_I[k] * scale + b[h]), causal.
+
+    Same parameters and initialisation as gsa_ref.py:75-95; ``forward`` returns
+    the [B, T, T] float32 score matrix with -inf above the diagonal
+    (gsa_ref.py:97-126), computed by ``gsa_indexer_scores``."""
+
+    def __init__(self, hidden_size: int, d_indexer: int = 64, n_idx_heads: int = 4):
+        super().__init__()
+        self.d_indexer = d_indexer
+        self.n_idx_heads = n_idx_heads
+        self.scale = 1.0 / math.sqrt(d_indexer)
+
+        self.idx_q_proj = nn.Linear(hidden_size, n_idx_heads * d_indexer, bias=False)
+        self.idx_k_proj = nn.Linear(hidden_size, d_indexer, bias=False)
+        self.idx_w_proj = nn.Linear(hidden_size, n_idx_heads, bias=True)
+        self.idx_bias = nn.Parameter(torch.zeros(n_idx_heads))
+
+        nn.init.xavier_uniform_(self.idx_q_proj.weight, gain=1.0)
+        nn.init.xavier_uniform_(self.idx_k_proj.weight, gain=1.0)
+        nn.init.xavier_uniform_(self.idx_w_proj.weight, gain=0.1)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, T, _ = x.shape
+        q_idx = self.idx_q_proj(x).view(B, T, self.n_idx_heads, self.d_indexer)
+        k_idx = self.idx_k_proj(x)
+        w = self.idx_w_proj(x)
+        return ops.fused_gated_indexer(q_idx, k_idx, w, self.idx_bias, self.scale, causal=True)
+
+
+# ── Top-k selector ─────────────────────────────────────────────────────────
+
+class AdaptiveTopKSelector(nn.Module):
+    """Fixed k_eff = min(k_base, k_max, T_kv) selection, as gsa_ref.py:131-150.
+
+    ``forward(scores)`` returns (indices int64 [B,T,k], mask bool [B,T,k], k_eff).
+    Indices come back in ascending order (the order gsa_opt.py:674-677 sorts
+    into); valid slots precede masked filler slots; ties go to the lower index.
+    ``k_min`` is stored for interface parity; the reference never reads it."""
+
+    def __init__(self, k_base: int = 2048, k_min: int = 256, k_max: int = 4096):
+        super().__init__()
+        self.k_base = k_base
+        self.k_min = k_min
+        self.k_max = k_max
+
+    def k_effective(self, t_kv: int) -> int:
+        return min(self.k_base, self.k_max, t_kv)
+
+    def forward(self, scores: torch.Tensor):
+        B, T, T_kv = scores.shape
+        k_eff = self.k_effective(T_kv)
+        # Every column is a candidate; -inf scores rank last and come back
+        # with mask False, whatever the pattern of -inf in the rows.
+        idx, mask, _ = ops.topk_select(scores.float().contiguous(), k_eff, q_pos0=T_kv,
+                                       want_bitmask=False)
+        return idx.long(), mask, k_eff
+
+
+# ── Gates ──────────────────────────────────────────────────────────────────
+
+class ValueGate(nn.Module):
+    """G2: v * sigmoid(W x + b), bias init 0.5 (gsa_ref.py:155-166)."""
+
+    def __init__(self, hidden_size: int):
+        super().__init__()
+        self.gate_proj = nn.Linear(hidden_size, hidden_size, bias=True)
+        nn.init.constant_(self.gate_proj.bias, 0.5)
+
+    def forward(self, v: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        B, T, H, d = v.shape
+        return ops.output_gate(v, self.gate_proj(x)).view(B, T, H, d)
+
+
+class OutputGate(nn.Module):
+    """G1: o * sigmoid(W x + b), bias init 0.5 (gsa_ref.py:169-180)."""
+
+    def __init__(self, hidden_size: int):
+        super().__init__()
+        self.gate_proj = nn.Linear(hidden_size, hidden_size, bias=True)
+        nn.init.constant_(self.gate_proj.bias, 0.5)
+
+    def forward(self, output: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        B, T, H, d = output.shape
+        return ops.output_gate(output, self.gate_proj(x)).view(B, T, H, d)
+
+
+# ── Main module ────────────────────────────────────────────────────────────
+
+class GatedSparseAttention(nn.Module):
+    """Gated Sparse Attention forward on B200 (see the module docstring)."""
+
+    def __init__(self, hidden_size: int, num_heads: int, k_max: int = 4096,
+                 d_indexer: int = 64, n_idx_heads: int = 4, k_base: int = 2048,
+                 k_min: int = 256):
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.num_heads = num_heads
+        self.d_head = hidden_size // num_heads
+        self.scale = self.d_head ** -0.5
+
+        self.q_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.k_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.v_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+        self.o_proj = nn.Linear(hidden_size, hidden_size, bias=False)
+
+        self.indexer = GatedLightningIndexer(hidden_size, d_indexer, n_idx_heads)
+        self.topk_selector = AdaptiveTopKSelector(k_base, k_min, k_max)
+        self.value_gate = ValueGate(hidden_size)
+        self.output_gate = OutputGate(hidden_size)
+        self.rotary_emb = RotaryEmbedding(self.d_head)
+
+        self._fused_weight: Optional[torch.Tensor] = None
+        self._fused_bias: Optional[torch.Tensor] = None
+        self._stage_events: Optional[list] = None
+        D, hi, di = hidden_size, n_idx_heads, d_indexer
+        # Column layout of the fused projection output (gsa_opt.py:562-571 order).
+        self._proj_sizes = [D, D, D, D, D, hi * di, di, hi]
+        offs, o = [], 0
+        for sz in self._proj_sizes:
+            offs.append(o)
+            o += sz
+        self._proj_offsets = offs
+        self._proj_total = o
+        # Padded so that every row of the GEMM output is 64-element aligned.
+        self._proj_padded = (o + 63) // 64 * 64
+
+    # ---------------------------------------------------------------- weights
+    def fuse_projections(self) -> None:
+        """Build the fused projection weight/bias.  Call again after changing weights."""
+        D = self.hidden_size
+        w = torch.cat([
+            self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
+            self.value_gate.gate_proj.weight, self.output_gate.gate_proj.weight,
+            self.indexer.idx_q_proj.weight, self.indexer.idx_k_proj.weight,
+            self.indexer.idx_w_proj.weight,
+        ], dim=0).detach()
+        pad = self._proj_padded - self._proj_total
+        if pad:
+            w = torch.cat([w, w.new_zeros(pad, D)], dim=0)
+        b = w.new_zeros(self._proj_padded)
+        o = self._proj_offsets
+        b[o[3]:o[3] + D] = self.value_gate.gate_proj.bias.detach()
+        b[o[4]:o[4] + D] = self.output_gate.gate_proj.bias.detach()
+        hi = self.indexer.n_idx_heads
+        b[o[7]:o[7] + hi] = self.indexer.idx_w_proj.bias.detach()
+        self._fused_weight = w.contiguous()
+        self._fused_bias = b.contiguous()
+
+    def _get_fused_weight(self):
+        p = self.q_proj.weight
+        if (self._fused_weight is None or self._fused_weight.device != p.device
+                or self._fused_weight.dtype != p.dtype):
+            self.fuse_projections()
+        return self._fused_weight, self._fused_bias
+
+    # ---------------------------------------------------------------- forward
+    def project(self, x: torch.Tensor) -> torch.Tensor:
+        """Fused projection GEMM: [B, T, D] -> [B, T, padded width] (cuBLAS)."""
+        B, T, D = x.shape
+        w, b = self._get_fused_weight()
+        out = torch.addmm(b, x.reshape(B * T, D), w.t())
+        return out.view(B, T, self._proj_padded)
+
+    def split(self, proj: torch.Tensor):
+        """Named column views of a fused projection output (no copies)."""
+        o, D = self._proj_offsets, self.hidden_size
+        hi, di = self.indexer.n_idx_heads, self.indexer.d_indexer
+        B, T, _ = proj.shape
+        return {
+            "q": proj[..., o[0]:o[0] + D], "k": proj[..., o[1]:o[1] + D],
+            "v": proj[..., o[2]:o[2] + D], "vg": proj[..., o[3]:o[3] + D],
+            "og": proj[..., o[4]:o[4] + D],
+            "iq": proj[..., o[5]:o[5] + hi * di].unflatten(-1, (hi, di)),
+            "ik": proj[..., o[6]:o[6] + di], "iw": proj[..., o[7]:o[7] + hi],
+        }
+
+    def attend_rows(self, parts: dict, k_all: torch.Tensor, v_all: torch.Tensor,
+                    ik_all: torch.Tensor, q_rows: torch.Tensor, q_pos0: int) -> torch.Tensor:
+        """Indexer -> top-k -> sparse attention (+ output gate) for a block of query rows.
+
+        ``parts`` holds the block's own projection views (``iq``, ``iw``, ``og``);
+        ``q_rows`` its RoPE'd queries [B, Tq, D]; ``k_all``/``v_all``/``ik_all``
+        cover keys [0, Tkv).  Row r of the block is sequence position q_pos0 + r.
+        Returns the gated attention output [B, Tq, D] (before o_proj)."""
+        B, Tq, D = q_rows.shape
+        Tkv = k_all.shape[1]
+        H = self.num_heads
+        k_eff = self.topk_selector.k_effective(Tkv)
+        with _Stage(self, "k:indexer", "gsa_b200/indexer"):
+            scores = ops.indexer_scores(parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias,
+                                        self.indexer.scale, q_pos0=q_pos0, tkv=Tkv,
+                                        fill_upper=False)
+        if q_rows.dtype == torch.bfloat16 and self.d_head == 128:
+            with _Stage(self, "k:topk", "gsa_b200/topk_select"):
+                _, _, bitmask = ops.topk_select(scores, k_eff, q_pos0=q_pos0, want_indices=False,
+                                                want_mask=False, want_bitmask=True)
+            with _Stage(self, "k:masked_attention", "gsa_b200/sparse_attn"):
+                out = ops.masked_attention(q_rows, k_all, v_all, bitmask, self.scale, H,
+                                           og=parts["og"], q_pos0=q_pos0)
+            return out
+        with _Stage(self, "k:topk", "gsa_b200/topk_select"):
+            idx, mask, _ = ops.topk_select(scores, k_eff, q_pos0=q_pos0, want_bitmask=False)
+        d = self.d_head
+        with _Stage(self, "k:gather_attention", "gsa_b200/sparse_attn"):
+            attn = ops.gather_attention(q_rows.view(B, Tq, H, d), k_all.view(B, Tkv, H, d),
+                                        v_all.view(B, Tkv, H, d), idx, mask, self.scale)
+        with _Stage(self, "k:output_gate", "gsa_b200/output_gate"):
+            out = ops.output_gate(attn.view(B, Tq, D), parts["og"])
+        return out
+
+    def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
+                ) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("gsa_b200.GatedSparseAttention runs on CUDA only (no CPU path)")
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            raise RuntimeError(f"unsupported dtype {x.dtype}")
+        B, T, D = x.shape
+        x = x.contiguous()
+        _nvtx_push("gsa_b200/forward")
+        with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
+            proj = self.project(x)
+        parts = self.split(proj)
+        cos, sin = self.rotary_emb(T, x.device, x.dtype)
+        with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
+            q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, self.num_heads,
+                                     v_src=parts["v"], vg_src=parts["vg"])
+        attn = self.attend_rows(parts, k, v, parts["ik"], q, q_pos0=0)
+        with _Stage(self, "lib:o_proj", "gsa_b200/o_proj"):
+            out = F.linear(attn.view(B, T, D), self.o_proj.weight)
+        _nvtx_pop()
+        return out

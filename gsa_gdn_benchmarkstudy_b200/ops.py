@@ -1,0 +1,256 @@
+"""Tensor-level wrappers over the C ABI (``include/gsa_b200.h``).
+
+Each function takes CUDA tensors, checks layouts, allocates its outputs with
+torch on the tensors' device and launches on ``torch.cuda.current_stream()``.
+There is no CPU path: a CPU tensor or a missing ``libgsa_b200.so`` raises.
+
+The op-level functions of the reference are mirrored with the same names and
+argument meaning:
+  * ``fused_gated_indexer``  — gsa_triton/gsa_opt.py:143-176
+  * ``fused_sparse_attention`` — gsa_triton/gsa_opt.py:349-383
+  * ``apply_rotary_pos_emb`` — gsa_triton/gsa_ref.py:35-40
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.GSA_DTYPE_BF16, torch.float32: _lib.GSA_DTYPE_F32}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise RuntimeError(f"gsa_b200 supports bfloat16 and float32, got {t.dtype}") from None
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("gsa_b200 runs only on CUDA tensors (no CPU fallback)")
+
+
+def _rows(t: torch.Tensor, width: int, name: str) -> int:
+    """Row stride (elements) of a [B, T, width]-shaped view with unit inner stride.
+
+    The batch stride must equal T * row stride (the C ABI convention)."""
+    if t.dim() != 3:
+        raise ValueError(f"{name}: expected 3 dims [B, T, {width}], got {tuple(t.shape)}")
+    B, T, W = t.shape
+    if W != width or t.stride(2) != 1:
+        raise ValueError(f"{name}: inner dim must be {width} contiguous elements")
+    rs = t.stride(1)
+    if B > 1 and t.stride(0) != T * rs:
+        raise ValueError(f"{name}: batch stride must equal T * row stride")
+    return rs
+
+
+def _flat_heads(t: torch.Tensor, name: str) -> torch.Tensor:
+    """View [B, T, H, d] (inner two dims contiguous) as [B, T, H*d]."""
+    if t.dim() == 3:
+        return t
+    if t.dim() != 4:
+        raise ValueError(f"{name}: expected [B, T, H, d] or [B, T, H*d]")
+    B, T, H, d = t.shape
+    if t.stride(3) != 1 or t.stride(2) != d:
+        t = t.contiguous()
+    return t.as_strided((B, T, H * d), (t.stride(0), t.stride(1), 1))
+
+
+def bitmask_words(tkv: int) -> int:
+    return int(_lib.load().gsa_bitmask_words(int(tkv)))
+
+
+# --------------------------------------------------------------------------- RoPE + G2
+def rope_gates(q_src: torch.Tensor, k_src: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+               num_heads: int, v_src: torch.Tensor | None = None,
+               vg_src: torch.Tensor | None = None):
+    """RoPE on q/k and (optionally) v * sigmoid(vg); all sources [B, T, H*d] with one row stride.
+
+    Returns (q, k, v) as contiguous [B, T, H*d] tensors (v is None without v_src)."""
+    _cuda(q_src, k_src, cos, sin, v_src, vg_src)
+    B, T, W = q_src.shape
+    d = W // num_heads
+    code = _dtype_code(q_src)
+    rs = _rows(q_src, W, "q_src")
+    for name, t in (("k_src", k_src), ("v_src", v_src), ("vg_src", vg_src)):
+        if t is not None:
+            if t.shape != q_src.shape or t.dtype != q_src.dtype or _rows(t, W, name) != rs:
+                raise ValueError(f"{name} must match q_src in shape, dtype and row stride")
+    if cos.shape != (T, d) or sin.shape != (T, d):
+        raise ValueError(f"cos/sin must be [T, d] = [{T}, {d}]")
+    cos = cos.to(q_src.dtype).contiguous()
+    sin = sin.to(q_src.dtype).contiguous()
+    q = torch.empty(B, T, W, device=q_src.device, dtype=q_src.dtype)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q) if v_src is not None else None
+    rc = _lib.load().gsa_rope_gates(
+        q_src.data_ptr(), k_src.data_ptr(),
+        v_src.data_ptr() if v_src is not None else None,
+        vg_src.data_ptr() if vg_src is not None else None,
+        rs, code, B, T, num_heads, d, cos.data_ptr(), sin.data_ptr(),
+        q.data_ptr(), k.data_ptr(), v.data_ptr() if v is not None else None, _stream())
+    _lib.check(rc, "gsa_rope_gates")
+    return q, k, v
+
+
+def apply_rotary_pos_emb(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """Reference-compatible RoPE: q, k [B, T, H, d]; cos, sin broadcastable to [1, T, 1, d]."""
+    B, T, H, d = q.shape
+    cos2 = cos.reshape(-1, d)[-T:] if cos.dim() != 2 else cos
+    sin2 = sin.reshape(-1, d)[-T:] if sin.dim() != 2 else sin
+    qe, ke, _ = rope_gates(_flat_heads(q, "q"), _flat_heads(k, "k"), cos2, sin2, H)
+    return qe.view(B, T, H, d), ke.view(B, T, H, d)
+
+
+# --------------------------------------------------------------------------- indexer
+def indexer_scores(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+                   scale: float, q_pos0: int = 0, tkv: int | None = None,
+                   fill_upper: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gated indexer scores [B, Tq, Tkv] fp32 (row stride padded to a multiple of 4).
+
+    q_idx [B, Tq, H_I, d_I] (or [B, Tq, H_I*d_I]), k_idx [B, Tkv, d_I], w [B, Tq, H_I];
+    query row r sits at sequence position q_pos0 + r."""
+    _cuda(q_idx, k_idx, w, bias)
+    if q_idx.dim() == 4:
+        B, Tq, H_I, d_I = q_idx.shape
+        if q_idx.stride(3) != 1 or q_idx.stride(2) != d_I:
+            q_idx = q_idx.contiguous()
+        q3 = q_idx.as_strided((B, Tq, H_I * d_I), (q_idx.stride(0), q_idx.stride(1), 1))
+    else:
+        raise ValueError("q_idx must be [B, Tq, H_I, d_I]")
+    Tkv = k_idx.shape[1] if tkv is None else tkv
+    d_code = _dtype_code(q_idx)
+    if k_idx.dtype != q_idx.dtype or w.dtype != q_idx.dtype:
+        raise ValueError("q_idx, k_idx and w must share a dtype")
+    qs = _rows(q3, H_I * d_I, "q_idx")
+    ks = _rows(k_idx, d_I, "k_idx")
+    ws = _rows(w, H_I, "w")
+    bias32 = bias.detach().to(torch.float32).contiguous()
+    stride = (Tkv + 3) // 4 * 4
+    if out is None:
+        out = torch.empty(B, Tq, stride, device=q_idx.device, dtype=torch.float32)
+    rc = _lib.load().gsa_indexer_scores(
+        q3.data_ptr(), qs, k_idx.data_ptr(), ks, w.data_ptr(), ws, bias32.data_ptr(),
+        float(scale), d_code, B, Tq, Tkv, int(q_pos0), H_I, d_I, out.data_ptr(), out.stride(1),
+        1 if fill_upper else 0, _stream())
+    _lib.check(rc, "gsa_indexer_scores")
+    return out[:, :, :Tkv]
+
+
+def fused_gated_indexer(q_idx, k_idx, w, bias, scale: float, causal: bool = True) -> torch.Tensor:
+    """Drop-in for gsa_opt.fused_gated_indexer: [B, T, T] fp32 with -inf above the diagonal.
+
+    causal=False places every query past the last key, so each row sees all keys."""
+    B, T = q_idx.shape[0], q_idx.shape[1]
+    Tkv = k_idx.shape[1]
+    s = indexer_scores(q_idx, k_idx, w, bias, scale, q_pos0=0 if causal else Tkv, tkv=Tkv,
+                       fill_upper=True)
+    return s.contiguous() if s.stride(1) != Tkv else s
+
+
+# --------------------------------------------------------------------------- top-k
+def topk_select(scores: torch.Tensor, k_sel: int, q_pos0: int = 0, want_indices: bool = True,
+                want_mask: bool = True, want_bitmask: bool = True):
+    """Top-k over causal rows of ``scores`` [B, Tq, Tkv] (fp32, unit inner stride).
+
+    Returns (indices int32 [B,Tq,k] ascending + masked filler, mask bool [B,Tq,k],
+    bitmask int32-storage uint32 words [B,Tq,W]); unrequested outputs are None."""
+    _cuda(scores)
+    if scores.dtype != torch.float32 or scores.dim() != 3 or scores.stride(2) != 1:
+        raise ValueError("scores must be float32 [B, Tq, Tkv] with unit inner stride")
+    B, Tq, Tkv = scores.shape
+    if B > 1 and scores.stride(0) != Tq * scores.stride(1):
+        raise ValueError("scores batch stride must equal Tq * row stride")
+    dev = scores.device
+    idx = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.int32) if want_indices else None
+    msk = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.uint8) if want_mask else None
+    W = bitmask_words(Tkv)
+    bm = torch.empty(B, Tq, W, device=dev, dtype=torch.int32) if want_bitmask else None
+    rc = _lib.load().gsa_topk_select(
+        scores.data_ptr(), scores.stride(1), B, Tq, Tkv, int(q_pos0), int(k_sel),
+        idx.data_ptr() if idx is not None else None, msk.data_ptr() if msk is not None else None,
+        bm.data_ptr() if bm is not None else None, W, _stream())
+    _lib.check(rc, "gsa_topk_select")
+    return idx, (msk.bool() if msk is not None else None), bm
+
+
+# --------------------------------------------------------------------------- attention
+def masked_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bitmask: torch.Tensor,
+                     scale: float, num_heads: int, og: torch.Tensor | None = None,
+                     q_pos0: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tensor-core sparse attention over a selection bitmask (bf16, d = 128).
+
+    q [B, Tq, H*d], k/v [B, Tkv, H*d], bitmask [B, Tq, W] from ``topk_select``;
+    og (optional) output-gate logits [B, Tq, H*d] fused as o * sigmoid(og)."""
+    q, k, v = _flat_heads(q, "q"), _flat_heads(k, "k"), _flat_heads(v, "v")
+    _cuda(q, k, v, bitmask, og)
+    B, Tq, W = q.shape
+    Tkv = k.shape[1]
+    d = W // num_heads
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError("masked_attention runs in bfloat16")
+    qs, ks, vs = _rows(q, W, "q"), _rows(k, W, "k"), _rows(v, W, "v")
+    if bitmask.dim() != 3 or bitmask.stride(2) != 1 or bitmask.shape[:2] != (B, Tq):
+        raise ValueError("bitmask must be [B, Tq, W] with unit inner stride")
+    ogs = _rows(og, W, "og") if og is not None else 0
+    if out is None:
+        out = torch.empty(B, Tq, W, device=q.device, dtype=q.dtype)
+    os_ = _rows(out, W, "out")
+    rc = _lib.load().gsa_masked_attention(
+        q.data_ptr(), qs, k.data_ptr(), ks, v.data_ptr(), vs, bitmask.data_ptr(),
+        bitmask.stride(1), og.data_ptr() if og is not None else None, ogs, out.data_ptr(), os_,
+        float(scale), B, Tq, Tkv, int(q_pos0), num_heads, d, _stream())
+    _lib.check(rc, "gsa_masked_attention")
+    return out
+
+
+def gather_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                     mask: torch.Tensor | None, scale: float) -> torch.Tensor:
+    """Index-gather sparse attention; q [B,Tq,H,d], k/v [B,Tkv,H,d], indices [B,Tq,k]."""
+    _cuda(q, k, v, indices, mask)
+    B, Tq, H, d = q.shape
+    Tkv = k.shape[1]
+    code = _dtype_code(q)
+    q3, k3, v3 = _flat_heads(q, "q"), _flat_heads(k, "k"), _flat_heads(v, "v")
+    W = H * d
+    qs, ks, vs = _rows(q3, W, "q"), _rows(k3, W, "k"), _rows(v3, W, "v")
+    idx = indices.to(torch.int32).contiguous()
+    k_sel = idx.shape[-1]
+    m = mask.to(torch.uint8).contiguous() if mask is not None else None
+    out = torch.empty(B, Tq, H, d, device=q.device, dtype=q.dtype)
+    rc = _lib.load().gsa_gather_attention(
+        q3.data_ptr(), qs, k3.data_ptr(), ks, v3.data_ptr(), vs, idx.data_ptr(),
+        m.data_ptr() if m is not None else None, k_sel, out.data_ptr(), W, float(scale), code,
+        B, Tq, Tkv, H, d, _stream())
+    _lib.check(rc, "gsa_gather_attention")
+    return out
+
+
+def fused_sparse_attention(q, k, v, indices, mask, scale: float) -> torch.Tensor:
+    """Drop-in for gsa_opt.fused_sparse_attention: [B, T, H, d] in q's dtype."""
+    return gather_attention(q, k, v, indices, mask, scale)
+
+
+def output_gate(o: torch.Tensor, og: torch.Tensor) -> torch.Tensor:
+    """o * sigmoid(og) element-wise (each op rounded to o's dtype); o, og [B, T, W]."""
+    _cuda(o, og)
+    if o.dim() == 4:
+        o = _flat_heads(o, "o")
+    B, T, W = o.shape
+    og = og.reshape(B, T, W)
+    code = _dtype_code(o)
+    o_s, g_s = _rows(o, W, "o"), _rows(og, W, "og")
+    out = torch.empty(B, T, W, device=o.device, dtype=o.dtype)
+    rows = B * T
+    rc = _lib.load().gsa_output_gate(o.data_ptr(), o_s, og.data_ptr(), g_s, out.data_ptr(), W,
+                                     code, rows, W, _stream())
+    _lib.check(rc, "gsa_output_gate")
+    return out

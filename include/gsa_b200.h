@@ -1,0 +1,203 @@
+/*
+ * gsa_b200.h — C ABI of the B200 (sm_100a) Gated Sparse Attention forward.
+ *
+ * Every entry point takes raw device pointers, element strides, sizes and a
+ * cudaStream_t passed as `void*` (NULL = legacy default stream).  Nothing in
+ * this library allocates device memory: outputs and scratch buffers are
+ * owned by the caller.  Every call returns a gsa_status_t; 0 means the work
+ * was enqueued on `stream`.  Launch failures are reported as GSA_ERR_CUDA
+ * and the CUDA error string is kept per host thread (gsa_last_error_string).
+ *
+ * Conventions shared by all entry points
+ *   - B      batch size.
+ *   - Tq     number of query rows handled by the call (a block of rows).
+ *   - Tkv    number of key rows (the full causal key range).
+ *   - q_pos0 absolute sequence position of query row 0 of the call; query
+ *            row r has position q_pos0 + r and sees keys j <= q_pos0 + r.
+ *            A whole-sequence call uses q_pos0 = 0 and Tq = Tkv.
+ *   - *_stride arguments are in ELEMENTS between consecutive sequence rows
+ *     of the same batch entry; batch entry b starts at b * T * stride.
+ *   - dtype: GSA_DTYPE_BF16 or GSA_DTYPE_F32 (the module's parameter dtype).
+ *
+ * The reference interface each entry point replaces is cited as
+ * file:line inside nirmalpratheep/GSA_GDN_BenchmarkStudy.
+ */
+#ifndef GSA_B200_H_
+#define GSA_B200_H_
+
+#include <stdint.h>
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define GSA_API __attribute__((visibility("default")))
+#else
+#define GSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GSA_OK = 0,
+  GSA_ERR_INVALID_ARG = 1,     /* null pointer, non-positive or inconsistent size */
+  GSA_ERR_ALIGNMENT = 2,       /* pointer or stride breaks a 16-byte rule */
+  GSA_ERR_UNSUPPORTED = 3,     /* shape/dtype this build does not implement */
+  GSA_ERR_CUDA = 4,            /* a CUDA runtime/driver call failed */
+  GSA_ERR_DEVICE_TIMEOUT = 5,  /* a bounded device-side wait expired */
+  GSA_ERR_NO_DEVICE = 6        /* no usable sm_100 device */
+} gsa_status_t;
+
+typedef enum { GSA_DTYPE_BF16 = 0, GSA_DTYPE_F32 = 1 } gsa_dtype_t;
+
+/* Library version, major*10000 + minor*100 + patch. */
+GSA_API int gsa_version(void);
+
+/* Human readable text for a status code (static storage). */
+GSA_API const char* gsa_status_string(int status);
+
+/* Text of the last CUDA error seen by a gsa_* call on this host thread. */
+GSA_API const char* gsa_last_error_string(void);
+
+/*
+ * Reads (and optionally clears) the device-side error word that kernels set
+ * when a bounded wait expires.  Synchronises the device.  *out receives 0 or
+ * a GSA_ERR_* code.
+ */
+GSA_API int gsa_device_error(int* out, int reset);
+
+/*
+ * Fused RoPE (q and k) + ValueGate (G2).  Replaces gsa_ref.py:283-298 (q/k/v
+ * views, ValueGate.forward at gsa_ref.py:163-166, apply_rotary_pos_emb at
+ * gsa_ref.py:35-40) and the track_B block of gsa_opt.py:683-696.
+ *
+ *   q_src, k_src, v_src, vg_src  [B, T, H*d] (dtype), all with row stride
+ *             src_stride; vg_src holds value-gate logits with the bias added.
+ *             v_src and vg_src may both be NULL: then only RoPE runs.
+ *   cos, sin  [T, d] (dtype) rotary tables; row t belongs to sequence row t
+ *             of every batch entry.
+ *   q_out, k_out, v_out  [B, T, H*d] contiguous (dtype).
+ *
+ *   q_out = dtype(dtype(q*cos) + dtype(rotate_half(q)*sin)), same for k,
+ *   v_out = dtype(v * dtype(sigmoid(vg)))
+ * Every product and sum is rounded to dtype where torch rounds it.
+ * d must be a multiple of 16; rows and sources 16-byte aligned.
+ */
+GSA_API int gsa_rope_gates(const void* q_src, const void* k_src,
+                           const void* v_src, const void* vg_src,
+                           int64_t src_stride, int dtype,
+                           int B, int T, int H, int d,
+                           const void* cos, const void* sin,
+                           void* q_out, void* k_out, void* v_out, void* stream);
+
+/*
+ * Gated lightning indexer scores.  Replaces GatedLightningIndexer.forward
+ * score math (gsa_ref.py:104-124) and the Triton kernel wrapper
+ * fused_gated_indexer (gsa_opt.py:143-176):
+ *
+ *   out[b,r,j] = sum_h sigmoid(w[b,r,h]) * sigmoid(q[b,r,h,:].k[b,j,:]*scale + bias[h])
+ *
+ * for j <= q_pos0 + r and j < Tkv; other columns are written only when
+ * fill_upper != 0 (then with -inf, as the reference's masked_fill).
+ *   q   [B, Tq, H_I, d_I] with row stride q_stride (dtype)
+ *   k   [B, Tkv, d_I] with row stride k_stride (dtype)
+ *   w   [B, Tq, H_I] with row stride w_stride (dtype; weight-proj bias added)
+ *   bias [H_I] float32
+ *   out [B, Tq, out_stride] float32, out_stride >= Tkv
+ * bf16: tcgen05 tensor-core kernel, requires H_I == 4, d_I == 64, 16-byte
+ * aligned rows.  f32: CUDA-core FFMA kernel (exact fp32 products).
+ */
+GSA_API int gsa_indexer_scores(const void* q, int64_t q_stride,
+                       const void* k, int64_t k_stride,
+                       const void* w, int64_t w_stride,
+                       const float* bias, float scale, int dtype,
+                       int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                       float* out, int64_t out_stride, int fill_upper,
+                       void* stream);
+
+/*
+ * Top-k selector over causal indexer scores.  Replaces
+ * AdaptiveTopKSelector.forward (gsa_ref.py:138-150, gsa_opt.py:473-483) and
+ * the index sort of gsa_opt.py:674-677.
+ *
+ * Row r has n = min(q_pos0 + r + 1, Tkv) valid scores (columns 0..n-1).
+ * If n <= k_sel all valid columns are selected, otherwise the k_sel largest,
+ * ties broken toward the lower column index.  Outputs (each may be NULL):
+ *   indices [B, Tq, k_sel] int32: selected columns in ascending order, then
+ *           (k_sel - selected) filler slots holding future positions
+ *           min(n + s, Tkv - 1) with mask 0 (the reference's -inf slots)
+ *   mask    [B, Tq, k_sel] uint8: 1 for selected slots
+ *   bitmask [B, Tq, bitmask_words] uint32: bit j set iff column j selected;
+ *           bitmask_words >= 4 * ceil(Tkv / 128), unused words written 0.
+ * scores: [B, Tq, score_stride] float32.
+ */
+GSA_API int gsa_topk_select(const float* scores, int64_t score_stride,
+                    int B, int Tq, int Tkv, int q_pos0, int k_sel,
+                    int32_t* indices, uint8_t* mask,
+                    uint32_t* bitmask, int64_t bitmask_words, void* stream);
+
+/* Number of uint32 words per row that gsa_topk_select / gsa_masked_attention
+ * expect for a key range of Tkv. */
+GSA_API int64_t gsa_bitmask_words(int Tkv);
+
+/*
+ * Sparse attention over a selection bitmask, on tcgen05 tensor cores.
+ * Replaces _gather_along_seq + sparse_attention_ref (gsa_ref.py:185-238),
+ * the Triton fused_sparse_attention (gsa_opt.py:349-383), and the output
+ * gate apply (gsa_ref.py:177-180 / gsa_opt.py:700,720) when og != NULL:
+ *
+ *   o[b,r,h,:] = softmax_{j : bit(b,r,j)} (q[b,r,h,:].k[b,j,h,:] * scale) . v[b,j,h,:]
+ *   out = og ? dtype(dtype(o) * dtype(sigmoid(og))) : dtype(o)
+ *
+ * A row with no selected key yields zeros (the reference's nan_to_num).
+ *   q   [B, Tq, H*d]  row stride q_stride (bf16)
+ *   k,v [B, Tkv, H*d] row strides k_stride, v_stride (bf16)
+ *   bitmask [B, Tq, bitmask_words] uint32 as written by gsa_topk_select
+ *   og  [B, Tq, H*d] output-gate logits (bias added), row stride og_stride, or NULL
+ *   out [B, Tq, H*d] row stride out_stride (bf16)
+ * Requires bf16, d == 128, 16-byte aligned rows.
+ */
+GSA_API int gsa_masked_attention(const void* q, int64_t q_stride,
+                         const void* k, int64_t k_stride,
+                         const void* v, int64_t v_stride,
+                         const uint32_t* bitmask, int64_t bitmask_words,
+                         const void* og, int64_t og_stride,
+                         void* out, int64_t out_stride,
+                         float scale, int B, int Tq, int Tkv, int q_pos0,
+                         int H, int d, void* stream);
+
+/*
+ * Index-gather sparse attention (any index lists, duplicates allowed).
+ * Replaces fused_sparse_attention (gsa_opt.py:349-383) / sparse_attention_ref
+ * (gsa_ref.py:202-238) for explicit (indices, mask) inputs.  Indices are
+ * clamped to [0, Tkv-1] as the reference does (gsa_ref.py:196); slots with
+ * mask 0 are skipped; a row with no valid slot yields zeros.
+ *   q [B, Tq, H, d], k/v [B, Tkv, H, d] with row strides (elements)
+ *   indices [B, Tq, k_sel] int32, mask [B, Tq, k_sel] uint8 (NULL = all 1)
+ *   out [B, Tq, H, d] row stride out_stride
+ * bf16 or f32; d in {64, 128, 256}.
+ */
+GSA_API int gsa_gather_attention(const void* q, int64_t q_stride,
+                         const void* k, int64_t k_stride,
+                         const void* v, int64_t v_stride,
+                         const int32_t* indices, const uint8_t* mask, int k_sel,
+                         void* out, int64_t out_stride,
+                         float scale, int dtype, int B, int Tq, int Tkv,
+                         int H, int d, void* stream);
+
+/*
+ * Element-wise output gate (G1) without attention, for callers that run
+ * gsa_gather_attention: out = dtype(o * dtype(sigmoid(og))).  Replaces
+ * OutputGate.forward's sigmoid/multiply (gsa_ref.py:177-180).
+ *   o, out [rows, width] with row strides; og [rows, width] row stride og_stride.
+ */
+GSA_API int gsa_output_gate(const void* o, int64_t o_stride,
+                    const void* og, int64_t og_stride,
+                    void* out, int64_t out_stride,
+                    int dtype, int rows, int width, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSA_B200_H_ */

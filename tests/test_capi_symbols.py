@@ -1,0 +1,60 @@
+"""The C-ABI library builds, loads without a GPU and exports every declared symbol."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from gsa_gdn_benchmarkstudy_b200 import _lib
+from gsa_gdn_benchmarkstudy_b200.build import build
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        names += re.findall(r"GSA_API\s+[\w\s\*]+?\b(gsa_\w+)\s*\(", h.read_text())
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_symbols()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+    # and the ctypes signature table covers exactly the declared set
+    assert set(names) == set(_lib.SIGNATURES)
+
+
+def test_host_only_entry_points(lib):
+    assert lib.gsa_version() >= 10000
+    assert lib.gsa_status_string(0) == b"ok"
+    assert lib.gsa_status_string(3) == b"unsupported shape or dtype"
+    assert lib.gsa_bitmask_words(1) == 4
+    assert lib.gsa_bitmask_words(128) == 4
+    assert lib.gsa_bitmask_words(129) == 8
+    assert lib.gsa_bitmask_words(16384) == 512
+
+
+def test_argument_checks_run_before_any_device_work(lib):
+    # Invalid sizes are rejected on the host with GSA_ERR_INVALID_ARG (1) /
+    # GSA_ERR_UNSUPPORTED (3) before the library touches CUDA.
+    rc = lib.gsa_topk_select(None, 0, 1, 1, 8, 0, 0, None, None, None, 0, None)
+    assert rc == 1
+    rc = lib.gsa_masked_attention(None, 0, None, 0, None, 0, None, 0, None, 0, None, 0,
+                                  1.0, 1, 1, 1, 0, 1, 64, None)
+    assert rc == 3
+    assert b"d == 128" in lib.gsa_last_error_string()
+    rc = lib.gsa_rope_gates(None, None, None, None, 0, 7, 1, 1, 1, 16, None, None, None, None,
+                            None, None)
+    assert rc == 3
+    # empty work is a no-op success
+    assert lib.gsa_indexer_scores(None, 0, None, 0, None, 0, None, 1.0, 0, 0, 4, 4, 0, 4, 64,
+                                  None, 4, 0, None) == 0
