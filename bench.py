@@ -220,9 +220,10 @@ def run_ours(args, cfg, rank: int, world: int, device):
     if world > 1:
         from gsa_gdn_benchmarkstudy_b200.sharding import ShardedGSA
         runner = ShardedGSA(model, dist.group.WORLD, T=cfg.T, B=cfg.B)
-        x_dev = runner.local_input(x_host.to(device))
+        x_local_host = runner.local_input(x_host).pin_memory()
+        x_dev = x_local_host.to(device)
         step = lambda: runner(x_dev)  # noqa: E731
-        e2e_step = lambda xh: runner.forward_host(xh)  # noqa: E731
+        e2e_step = lambda: runner.forward_host(x_local_host)  # noqa: E731
     else:
         x_dev = x_host.to(device)
         step = lambda: model(x_dev)  # noqa: E731
@@ -284,7 +285,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
             out = model(xd)
             out_host.copy_(out, non_blocking=True)
         else:
-            e2e_step(x_host)
+            e2e_step()
         e2e_ev[i][1].record(stream)
     torch.cuda.synchronize()
     e2e_local = sum(a.elapsed_time(b) for a, b in e2e_ev)
@@ -292,7 +293,8 @@ def run_ours(args, cfg, rank: int, world: int, device):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = t.item() / args.steps
-    h2d = x_host.numel() * x_host.element_size() // (world if world > 1 else 1) * (world if world > 1 else 1)
+    # bytes copied per step by rank 0: its input share in, the full output out
+    h2d = x_host.numel() * x_host.element_size() // world
     d2h = out_host.numel() * out_host.element_size()
 
     if rank != 0:

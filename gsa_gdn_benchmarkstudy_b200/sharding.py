@@ -1,0 +1,158 @@
+"""Multi-GPU GSA forward: one process per GPU, torch.distributed (NCCL) plumbing.
+
+The reference runs on one device only; this module partitions the forward.
+
+* B == 1 (long sequences): causally load-balanced query-row sharding.  The
+  sequence is cut into 2P equal blocks and rank r owns blocks r and 2P-1-r
+  (a cheap early block and an expensive late one: indexer work per row grows
+  with the row position, so the pair costs the same on every rank).  Each rank
+  projects only its own rows, applies RoPE / value gate, then all-gathers the
+  keys, values and indexer keys (k, v, k_I) so every rank holds [0, T).  Each
+  row's indexer, top-k and attention need nothing else, so there is no further
+  exchange until the output rows are all-gathered at the end.
+* B > 1 (batched serving): sequences are independent; rank r runs B/P of them
+  and the outputs are all-gathered.
+
+Only NCCL collectives cross GPUs (no peer-memory loads of any kind).
+"""
+from __future__ import annotations
+
+from typing import List, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import ops
+
+Block = Tuple[int, int]
+
+
+def zigzag_blocks(T: int, world: int, rank: int) -> List[Block]:
+    """Blocks [start, end) owned by ``rank``: r and 2P-1-r of 2P equal blocks."""
+    nb = 2 * world
+    if T % nb:
+        raise ValueError(f"T={T} must be a multiple of 2*world={nb} for row sharding")
+    b = T // nb
+    return [(rank * b, (rank + 1) * b), ((nb - 1 - rank) * b, (nb - rank) * b)]
+
+
+def causal_row_cost(blocks: Sequence[Block], k: int) -> Tuple[int, int]:
+    """(indexer pairs, attention pairs) of a set of row blocks: sum of t+1 and min(t+1, k)."""
+    idx = att = 0
+    for s, e in blocks:
+        idx += (e * (e + 1) - s * (s + 1)) // 2
+        # rows t in [s, e): min(t+1, k)
+        lo, hi = s, min(e, k)
+        if hi > lo:
+            att += (hi * (hi + 1) - lo * (lo + 1)) // 2
+        att += max(0, e - max(s, k)) * k
+    return idx, att
+
+
+def all_gather_equal(t: torch.Tensor, group) -> torch.Tensor:
+    """All-gather equally shaped tensors -> [world, *t.shape] (NCCL or gloo)."""
+    world = dist.get_world_size(group)
+    t = t.contiguous()
+    out = torch.empty((world, *t.shape), dtype=t.dtype, device=t.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), t, group=group)
+    return out
+
+
+def gather_rows(local: torch.Tensor, T: int, group) -> torch.Tensor:
+    """Reassemble zig-zag row shards [1, Tl, W] from every rank into [1, T, W] in sequence order."""
+    world = dist.get_world_size(group)
+    g = all_gather_equal(local[0], group)  # [world, Tl, W]
+    full = torch.empty((1, T, local.shape[-1]), dtype=local.dtype, device=local.device)
+    for r in range(world):
+        off = 0
+        for s, e in zigzag_blocks(T, world, r):
+            full[0, s:e] = g[r, off:off + (e - s)]
+            off += e - s
+    return full
+
+
+def gather_batch(local: torch.Tensor, group) -> torch.Tensor:
+    """Reassemble batch shards [B/P, T, W] into [B, T, W]."""
+    g = all_gather_equal(local, group)
+    return g.reshape(-1, *local.shape[1:])
+
+
+class ShardedGSA:
+    """Runs a GatedSparseAttention forward sharded over the ranks of ``group``.
+
+    ``local_input(x)`` picks this rank's share of a full input; ``__call__``
+    takes that share (on this rank's GPU) and returns the FULL output on every
+    rank; ``forward_host(x_host)`` does the same from pinned host memory."""
+
+    def __init__(self, model, group, T: int, B: int):
+        self.model = model
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.T, self.B = T, B
+        self.mode = "rows" if B == 1 else "batch"
+        if self.mode == "rows":
+            self.blocks = zigzag_blocks(T, self.world, self.rank)
+        else:
+            if B % self.world:
+                raise ValueError(f"B={B} must be a multiple of world={self.world}")
+            per = B // self.world
+            self.b0, self.b1 = self.rank * per, (self.rank + 1) * per
+        self._pos = None
+        self._host_out = None
+
+    # ---------------------------------------------------------------- inputs
+    def local_input(self, x: torch.Tensor) -> torch.Tensor:
+        if self.mode == "rows":
+            return torch.cat([x[:, s:e] for s, e in self.blocks], dim=1).contiguous()
+        return x[self.b0:self.b1].contiguous()
+
+    def _positions(self, device) -> torch.Tensor:
+        if self._pos is None or self._pos.device != device:
+            self._pos = torch.cat([torch.arange(s, e) for s, e in self.blocks]).to(device)
+        return self._pos
+
+    # ---------------------------------------------------------------- forward
+    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
+        if self.mode == "batch":
+            return gather_batch(self.model(x_local), self.group)
+        return self._forward_rows(x_local)
+
+    def _forward_rows(self, x_loc: torch.Tensor) -> torch.Tensor:
+        m = self.model
+        T, D, H = self.T, m.hidden_size, m.num_heads
+        proj = m.project(x_loc)
+        parts = m.split(proj)
+        cos, sin = m.rotary_emb(T, x_loc.device, x_loc.dtype)
+        pos = self._positions(x_loc.device)
+        q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
+                                 sin.index_select(0, pos), H, v_src=parts["v"],
+                                 vg_src=parts["vg"])
+        # keys, values and indexer keys of the whole sequence on every rank
+        k_full = gather_rows(k, T, self.group)
+        v_full = gather_rows(v, T, self.group)
+        ik_full = gather_rows(parts["ik"].contiguous(), T, self.group)
+        outs, off = [], 0
+        for s, e in self.blocks:
+            n = e - s
+            pb = {key: parts[key][:, off:off + n] for key in ("iq", "iw", "og")}
+            outs.append(m.attend_rows(pb, k_full[:, :e], v_full[:, :e], ik_full[:, :e],
+                                      q[:, off:off + n], q_pos0=s))
+            off += n
+        attn = torch.cat(outs, dim=1)
+        out_local = F.linear(attn, m.o_proj.weight)
+        return gather_rows(out_local, T, self.group)
+
+    def forward_host(self, x_local_host: torch.Tensor) -> torch.Tensor:
+        """This rank's input share from pinned host memory -> device, sharded forward,
+        full output read back into a pinned host buffer (returned)."""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        out = self(x_local_host.to(dev, non_blocking=True))
+        if self._host_out is None or self._host_out.shape != out.shape:
+            self._host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        self._host_out.copy_(out, non_blocking=True)
+        return self._host_out

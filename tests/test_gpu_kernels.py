@@ -53,7 +53,8 @@ def test_rope_gates_matches_reference_rounding(dtype):
     assert torch.equal(kg.cpu().view(B, T, H, d), ko)
     # the gate may differ by one ulp where sigmoid's float value rounds differently
     diff = (vgd.cpu().float() - vo.float()).abs()
-    ulp = vo.float().abs() * (2 ** -7 if dtype == torch.bfloat16 else 2 ** -22) + 1e-30
+    # one bf16 ulp; for fp32 a few ulps (the float sigmoid itself differs by 1-2 ulps)
+    ulp = vo.float().abs() * (2 ** -7 if dtype == torch.bfloat16 else 2 ** -20) + 1e-30
     assert bool((diff <= ulp).all())
     assert (diff > 0).float().mean() < 0.02
 
