@@ -14,19 +14,32 @@
 // of gathering 2*k*H*d bytes per query row as the reference does.
 //
 // CTA = (batch b, head h, 128-query tile).  Warp roles:
-//   warps 0-3  softmax + epilogue (thread = query row = TMEM lane)
-//   warp 4     TMA producer (Q once; K and V 128x128 tiles, 2-stage rings)
-//   warp 5     TMEM owner + single-thread tcgen05.mma issuer
-// Two passes over the key tiles (exact, no running rescale):
-//   pass 1: S = Q.K^T into one of two TMEM S buffers; softmax warps take the
-//           row max over selected keys.
-//   pass 2: S again; p = 2^((s - m) * scale * log2 e) for selected keys, 0
-//           otherwise; row sum l in fp32; P (bf16) written to shared memory in
-//           the 128B-swizzled K-major layout; O += P.V accumulates in TMEM.
-// Epilogue: o = O / l, rounded to bf16; optional gate bf16(o * bf16(sigmoid(og))).
+//   warps 0-7  softmax + epilogue.  Warp w serves query rows 32(w%4)..+31
+//              (TMEM lane quarter w%4) over the key tiles of parity w/4:
+//              even tiles go to warps 0-3, odd tiles to warps 4-7, so each SM
+//              sub-partition runs two softmax warps on different tiles with no
+//              per-tile synchronisation between them.  Each parity keeps its own
+//              running max m, row sum l and TMEM accumulator O_par; the two are
+//              merged once in the epilogue.
+//   warp 8     TMA producer (Q once; K and V 128x128 tiles, 2-stage rings)
+//   warp 9     TMEM owner + single-thread tcgen05.mma issuer
+// Per key tile j (parity par = j % 2):
+//   MMA:      S_j = Q.K_j^T into TMEM S buffer par (issued one tile ahead);
+//             O_par += P_j.V_j once P_j is in shared memory.
+//   softmax:  p = 2^(s*c - m*c), c = scale*log2(e), for selected keys, using the
+//             running max m of this parity without waiting for the tile max.
+//             m is raised only when some selected s*c - m*c exceeds 8 (p > 256):
+//             then the warp recomputes the tile's p from S with the new m and
+//             scales l and its rows of O_par by 2^((m_old - m_new)*c); the P.V of
+//             the previous tile of the same parity has finished by then.  A
+//             row's first selected keys set m from an exact tile max.
+//             P (bf16) goes to shared buffer par in the 128B-swizzled K-major
+//             layout the MMA reads.
+// Epilogue: M = max(m_even, m_odd), O = O_even*2^((m_even-M)c) + O_odd*2^((m_odd-M)c)
+//   (likewise l), o = O / l rounded to bf16; optional gate bf16(o * bf16(sigmoid(og))).
 //
-// TMEM: S0 [0,128), S1 [128,256), O [256,384) fp32 columns (512 allocated).
-// Shared memory: Q 32 KB, K 2x32 KB, V 2x32 KB, P 32 KB (one CTA per SM).
+// TMEM: S0 [0,128), S1 [128,256), O_even [256,384), O_odd [384,512) fp32 columns.
+// Shared memory: Q 32 KB, K 2x32 KB, V 2x32 KB, P 2x32 KB + control (one CTA per SM).
 #include "kernels.h"
 
 namespace gsa {
@@ -37,20 +50,26 @@ constexpr int kAtBN = 128;
 constexpr int kAtD = 128;
 constexpr int kAtTileBytes = kAtBM * kAtD * 2;  // 32 KB: two 128x64 swizzled boxes
 constexpr int kAtBoxBytes = kAtTileBytes / 2;   // 16 KB
-constexpr int kAtThreads = 192;
+constexpr int kAtThreads = 320;
 constexpr int kAtTmemCols = 512;
+constexpr float kRescaleLog2 = 8.0f;            // p may reach 2^8 before m is raised
 
 struct AtSmem {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, p_empty;
+  uint64_t p_full[2], p_empty[2];
   uint64_t o_full;
   uint32_t tmem_base;
   int abort;
+  float xm[2][kAtBM];  // [parity][row] running max, for the epilogue merge
+  float xl[2][kAtBM];  // [parity][row] row sum
 };
-constexpr int kAtSmemBytes = 1024 + 6 * kAtTileBytes + 256;
+// The dynamic shared memory base is 1024-byte aligned (checked at run time),
+// so the swizzled tiles need no alignment slack: 7 tiles + the control block.
+constexpr int kAtSmemBytes = 7 * kAtTileBytes + ((sizeof(AtSmem) + 15) / 16) * 16;
+static_assert(kAtSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -63,14 +82,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     masked_attn_kernel(const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap,
                        const __grid_constant__ CUtensorMap vmap, MaskedAttnArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // swizzled TMA/MMA tiles need 1024 B alignment
+    if (threadIdx.x == 0) atomicExch(a.err, GSA_ERR_ALIGNMENT);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* q_s = smem;
   uint8_t* k_s = smem + kAtTileBytes;      // 2 stages
   uint8_t* v_s = smem + 3 * kAtTileBytes;  // 2 stages
-  uint8_t* p_s = smem + 5 * kAtTileBytes;
-  AtSmem* sh = reinterpret_cast<AtSmem*>(smem + 6 * kAtTileBytes);
+  uint8_t* p_s = smem + 5 * kAtTileBytes;  // 2 buffers
+  AtSmem* sh = reinterpret_cast<AtSmem*>(smem + 7 * kAtTileBytes);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -92,14 +114,14 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(&sh->v_empty[s], 1);
       mbar_init(&sh->s_full[s], 1);
       mbar_init(&sh->s_empty[s], 4);
+      mbar_init(&sh->p_full[s], 4);
+      mbar_init(&sh->p_empty[s], 1);
     }
-    mbar_init(&sh->p_full, 4);
-    mbar_init(&sh->p_empty, 1);
     mbar_init(&sh->o_full, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(&sh->tmem_base, kAtTmemCols);
     tmem_relinquish();
   }
@@ -109,7 +131,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const uint32_t tmem = sh->tmem_base;
   volatile int* abort = &sh->abort;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&qmap);
@@ -119,189 +141,220 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_arrive_expect_tx(&sh->q_full, kAtTileBytes);
       tma_load_3d(q_s, &qmap, x0, row0, b, &sh->q_full);
       tma_load_3d(q_s + kAtBoxBytes, &qmap, x0 + 64, row0, b, &sh->q_full);
-      int kit = 0, vit = 0;
-      bool ok = true;
-      for (int pass = 0; pass < 2 && ok; ++pass) {
-        for (int j = 0; j < nt; ++j) {
-          {
-            const int st = kit & 1;
-            if (!mbar_wait(&sh->k_empty[st], ((kit >> 1) & 1) ^ 1, a.err, abort)) { ok = false; break; }
-            uint8_t* dst = k_s + st * kAtTileBytes;
-            mbar_arrive_expect_tx(&sh->k_full[st], kAtTileBytes);
-            tma_load_3d(dst, &kmap, x0, j * kAtBN, b, &sh->k_full[st]);
-            tma_load_3d(dst + kAtBoxBytes, &kmap, x0 + 64, j * kAtBN, b, &sh->k_full[st]);
-            ++kit;
-          }
-          if (pass == 1) {
-            const int st = vit & 1;
-            if (!mbar_wait(&sh->v_empty[st], ((vit >> 1) & 1) ^ 1, a.err, abort)) { ok = false; break; }
-            uint8_t* dst = v_s + st * kAtTileBytes;
-            mbar_arrive_expect_tx(&sh->v_full[st], kAtTileBytes);
-            tma_load_3d(dst, &vmap, x0, j * kAtBN, b, &sh->v_full[st]);
-            tma_load_3d(dst + kAtBoxBytes, &vmap, x0 + 64, j * kAtBN, b, &sh->v_full[st]);
-            ++vit;
-          }
-        }
+      for (int j = 0; j < nt; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = ((j >> 1) & 1) ^ 1;
+        if (!mbar_wait(&sh->k_empty[st], ph, a.err, abort)) break;
+        uint8_t* kd = k_s + st * kAtTileBytes;
+        mbar_arrive_expect_tx(&sh->k_full[st], kAtTileBytes);
+        tma_load_3d(kd, &kmap, x0, j * kAtBN, b, &sh->k_full[st]);
+        tma_load_3d(kd + kAtBoxBytes, &kmap, x0 + 64, j * kAtBN, b, &sh->k_full[st]);
+        if (!mbar_wait(&sh->v_empty[st], ph, a.err, abort)) break;
+        uint8_t* vd = v_s + st * kAtTileBytes;
+        mbar_arrive_expect_tx(&sh->v_full[st], kAtTileBytes);
+        tma_load_3d(vd, &vmap, x0, j * kAtBN, b, &sh->v_full[st]);
+        tma_load_3d(vd + kAtBoxBytes, &vmap, x0 + 64, j * kAtBN, b, &sh->v_full[st]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(kAtBM, kAtBN, 0, 0);   // Q K-major, K K-major
-      constexpr uint32_t idesc_o = idesc_bf16_f32(kAtBM, kAtD, 0, 1);    // P K-major, V MN-major
+      constexpr uint32_t idesc_s = idesc_bf16_f32(kAtBM, kAtBN, 0, 0);  // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_bf16_f32(kAtBM, kAtD, 0, 1);   // P K-major, V MN-major
       const uint32_t q_base = smem_u32(q_s);
       const uint32_t k_base = smem_u32(k_s);
       const uint32_t v_base = smem_u32(v_s);
       const uint32_t p_base = smem_u32(p_s);
-      int sit = 0, kit = 0, vit = 0;
       bool ok = mbar_wait(&sh->q_full, 0, a.err, abort);
 
-      auto issue_s = [&]() -> bool {
-        const int sb = sit & 1, st = kit & 1;
-        if (!mbar_wait(&sh->k_full[st], (kit >> 1) & 1, a.err, abort)) return false;
-        if (!mbar_wait(&sh->s_empty[sb], ((sit >> 1) & 1) ^ 1, a.err, abort)) return false;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&sh->k_full[st], ph, a.err, abort)) return false;
+        if (!mbar_wait(&sh->s_empty[st], ph ^ 1, a.err, abort)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kAtD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kAtBoxBytes + (kk & 3) * 32;
           const uint64_t ad = sdesc_sw128(q_base + off, 16, 1024);
           const uint64_t bd = sdesc_sw128(k_base + st * kAtTileBytes + off, 16, 1024);
-          tc_mma_ss(tmem + sb * kAtBN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          tc_mma_ss(tmem + st * kAtBN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&sh->s_full[sb]);
+        tc_commit(&sh->s_full[st]);
         tc_commit(&sh->k_empty[st]);
-        ++sit;
-        ++kit;
         return true;
       };
 
-      // pass 1: scores only
-      for (int j = 0; ok && j < nt; ++j) ok = issue_s();
-      // pass 2: scores again, then O += P.V once the softmax warps wrote P
-      if (ok) ok = issue_s();
+      if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < nt; ++j) {
-        if (j + 1 < nt) {
-          ok = issue_s();
-          if (!ok) break;
-        }
-        const int vst = vit & 1;
-        if (!mbar_wait(&sh->v_full[vst], (vit >> 1) & 1, a.err, abort)) { ok = false; break; }
-        if (!mbar_wait(&sh->p_full, j & 1, a.err, abort)) { ok = false; break; }
+        if (j + 1 < nt && !(ok = issue_s(j + 1))) break;
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&sh->v_full[st], ph, a.err, abort)) { ok = false; break; }
+        if (!mbar_wait(&sh->p_full[st], ph, a.err, abort)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kAtBN / 16; ++kk) {
-          const uint64_t ad =
-              sdesc_sw128(p_base + (kk >> 2) * kAtBoxBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_sw128(
+              p_base + st * kAtTileBytes + (kk >> 2) * kAtBoxBytes + (kk & 3) * 32, 16, 1024);
           const uint64_t bd =
-              sdesc_sw128(v_base + vst * kAtTileBytes + kk * 16 * 128, kAtBoxBytes, 1024);
-          tc_mma_ss(tmem + 2 * kAtBN, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+              sdesc_sw128(v_base + st * kAtTileBytes + kk * 16 * 128, kAtBoxBytes, 1024);
+          tc_mma_ss(tmem + (2 + st) * kAtBN, ad, bd, idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(&sh->p_empty);
-        tc_commit(&sh->v_empty[vst]);
-        ++vit;
+        tc_commit(&sh->p_empty[st]);
+        tc_commit(&sh->v_empty[st]);
       }
       if (ok) tc_commit(&sh->o_full);
     }
     __syncwarp();
   } else {
     // ---------------------------------------------------------- softmax warps
-    const int i = tid;
+    const int quarter = warp & 3;
+    const int par = warp >> 2;           // key-tile parity served by this warp
+    const int i = quarter * 32 + lane;   // query row in the tile == TMEM lane
     const int r = row0 + i;
     const bool row_ok = r < a.Tq;
     const int64_t grow = static_cast<int64_t>(b) * a.Tq + r;
-    const uint32_t* bm = a.bitmask + grow * a.bitmask_words;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint4* bm = reinterpret_cast<const uint4*>(a.bitmask + grow * a.bitmask_words);
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_taddr = tmem + lane_base + par * kAtBN;
+    const uint32_t o_taddr = tmem + lane_base + (2 + par) * kAtBN;
     const float c = a.scale * 1.4426950408889634f;
-    const uint32_t p_row = smem_u32(p_s);
-    int sit = 0;
+    const uint32_t pb = smem_u32(p_s) + par * kAtTileBytes;
     bool ok = true;
+    float m = -INFINITY;   // running max of this parity (raw dot-product units)
+    float l = 0.f;         // row sum of this parity, relative to m
+    uint4 bits_next = (row_ok && par < nt) ? bm[par] : make_uint4(0, 0, 0, 0);
 
-    // pass 1: row max over selected keys (raw dot-product units)
-    float m = -INFINITY;
-    for (int j = 0; j < nt; ++j) {
-      const int sb = sit & 1;
-      uint4 bits = make_uint4(0, 0, 0, 0);
-      if (row_ok) bits = *reinterpret_cast<const uint4*>(bm + j * 4);
-      if (!mbar_wait_warp(&sh->s_full[sb], (sit >> 1) & 1, a.err, abort)) { ok = false; break; }
+    for (int j = par; ok && j < nt; j += 2) {
+      const uint32_t ph = (j >> 1) & 1;
+      const uint4 bits = bits_next;
+      if (row_ok && j + 2 < nt) bits_next = bm[j + 2];
+      const uint32_t wb[4] = {bits.x, bits.y, bits.z, bits.w};
+      if (!(ok = mbar_wait_warp(&sh->s_full[par], ph, a.err, abort))) break;
       tc_fence_after();
-      const uint32_t wbits[4] = {bits.x, bits.y, bits.z, bits.w};
+      // a row's first selected keys: take the exact tile max to start m
+      if (__any_sync(0xFFFFFFFFu, row_ok && m == -INFINITY)) {
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + sb * kAtBN + cc * 32, raw);
-        tc_wait_ld();
-        const uint32_t wb = wbits[cc];
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t sv[32];
+          tmem_ld32(s_taddr + cc * 32, sv);
+          tc_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if ((wb >> e) & 1u) m = fmaxf(m, __uint_as_float(raw[e]));
+          for (int e = 0; e < 32; ++e)
+            if ((wb[cc] >> e) & 1u) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sv[e]));
+        }
+        if (m == -INFINITY) m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh->s_empty[sb]);
-      ++sit;
-    }
-    if (m == -INFINITY) m = 0.f;
-    const float mc = m * c;
+      // P buffer par is free (and O_par stable) once P.V of tile j-2 finished
+      if (!(ok = mbar_wait_warp(&sh->p_empty[par], ph ^ 1, a.err, abort))) break;
 
-    // pass 2: probabilities, P tile, row sum
-    float l = 0.f;
-    for (int j = 0; ok && j < nt; ++j) {
-      const int sb = sit & 1;
-      uint4 bits = make_uint4(0, 0, 0, 0);
-      if (row_ok) bits = *reinterpret_cast<const uint4*>(bm + j * 4);
-      if (!mbar_wait_warp(&sh->s_full[sb], (sit >> 1) & 1, a.err, abort)) { ok = false; break; }
-      tc_fence_after();
-      // P of the previous tile must have been consumed by its P.V MMA.
-      if (!mbar_wait_warp(&sh->p_empty, (j & 1) ^ 1, a.err, abort)) { ok = false; break; }
-      const uint32_t wbits[4] = {bits.x, bits.y, bits.z, bits.w};
+      // p = 2^(s*c - m*c) with the running max; returns this tile's row sum
+      // and the largest exponent s*c - m*c among selected keys
+      auto exp_pass = [&](float& amax) -> float {
+        const float mc = (m == -INFINITY) ? 0.f : m * c;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        float a4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + sb * kAtBN + cc * 32, raw);
-        tc_wait_ld();
-        const uint32_t wb = wbits[cc];
-        uint32_t packed[16];
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t sv[32];
+          tmem_ld32(s_taddr + cc * 32, sv);
+          tc_wait_ld();
+          uint32_t packed[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = 0.f, p1 = 0.f;
-          if ((wb >> e) & 1u) p0 = fast_ex2(fmaf(__uint_as_float(raw[e]), c, -mc));
-          if ((wb >> (e + 1)) & 1u) p1 = fast_ex2(fmaf(__uint_as_float(raw[e + 1]), c, -mc));
-          l += p0;
-          l += p1;
-          packed[e >> 1] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 32; e += 2) {
+            float p0 = 0.f, p1 = 0.f;
+            if ((wb[cc] >> e) & 1u) {
+              const float x = fmaf(__uint_as_float(sv[e]), c, -mc);
+              a4[e & 3] = fmaxf(a4[e & 3], x);
+              p0 = fast_ex2(x);
+            }
+            if ((wb[cc] >> (e + 1)) & 1u) {
+              const float x = fmaf(__uint_as_float(sv[e + 1]), c, -mc);
+              a4[(e + 1) & 3] = fmaxf(a4[(e + 1) & 3], x);
+              p1 = fast_ex2(x);
+            }
+            l4[(e >> 1) & 3] += p0 + p1;
+            packed[e >> 1] = pack_bf16x2(p0, p1);
+          }
+          // keys 32cc..32cc+31 -> box cc/2, 16-byte chunks 4*(cc%2) .. +3 of row i
+          const uint32_t box = pb + (cc >> 1) * kAtBoxBytes;
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd)
+            st_shared_v4(box + sw128_offset(i, (cc & 1) * 4 + qd), packed[4 * qd],
+                         packed[4 * qd + 1], packed[4 * qd + 2], packed[4 * qd + 3]);
         }
-        // keys 32cc..32cc+31 -> box cc/2, 16-byte chunks 4*(cc%2) .. +3 of row i
-        const uint32_t box = p_row + (cc >> 1) * kAtBoxBytes;
+        amax = fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3]));
+        return (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      };
+      float amax;
+      float lt = exp_pass(amax);
+      // rows whose p overshot 2^8: raise m to the tile max, rescale, redo the tile
+      const bool over = amax > kRescaleLog2;
+      if (__any_sync(0xFFFFFFFFu, over)) {
+        const float alpha = over ? fast_ex2(-amax) : 1.f;  // 2^((m_old - m_new) c)
+        if (over) m += amax / c;
+        l *= alpha;
+        if (j >= 2) {  // O_par holds P.V of earlier tiles of this parity
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t ov[32];
+            tmem_ld32(o_taddr + cc * 32, ov);
+            tc_wait_ld();
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          const uint32_t chunk = (cc & 1) * 4 + qd;
-          st_shared_v4(box + sw128_offset(i, chunk), packed[4 * qd], packed[4 * qd + 1],
-                       packed[4 * qd + 2], packed[4 * qd + 3]);
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st32(o_taddr + cc * 32, ov);
+          }
+          tc_wait_st();
         }
+        lt = exp_pass(amax);
       }
-      tc_fence_before();
+      l += lt;
       fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sh->s_empty[sb]);
-        mbar_arrive(&sh->p_full);
+        mbar_arrive(&sh->s_empty[par]);  // S_j consumed
+        mbar_arrive(&sh->p_full[par]);   // P_j ready
       }
-      ++sit;
     }
 
-    // epilogue: O / l (+ output gate), bf16 store
-    if (ok && mbar_wait_warp(&sh->o_full, 0, a.err, abort)) {
+    // epilogue: merge the two parities, O / l (+ output gate), bf16 store of
+    // this warp's 64 output channels (par * 64 ..)
+    sh->xm[par][i] = m;
+    sh->xl[par][i] = l;
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+    const float m_e = sh->xm[0][i], m_o = sh->xm[1][i];
+    const float mm = fmaxf(m_e, m_o);
+    const float a_e = m_e == -INFINITY ? 0.f : fast_ex2((m_e - mm) * c);
+    const float a_o = m_o == -INFINITY ? 0.f : fast_ex2((m_o - mm) * c);
+    const float lsum = sh->xl[0][i] * a_e + sh->xl[1][i] * a_o;
+    const bool odd_written = nt > 1;  // O_odd is only written when tile 1 exists
+    ok = ok && mbar_wait_warp(&sh->o_full, 0, a.err, abort);
+    if (ok) {
       tc_fence_after();
-      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out) + grow * a.out_stride + h * kAtD;
+      const float inv_l = lsum > 0.f ? 1.0f / lsum : 0.f;
+      const uint32_t col0 = par * 64;
+      __nv_bfloat16* orow =
+          static_cast<__nv_bfloat16*>(a.out) + grow * a.out_stride + h * kAtD + col0;
       const __nv_bfloat16* grow_p =
-          a.og ? static_cast<const __nv_bfloat16*>(a.og) + grow * a.og_stride + h * kAtD : nullptr;
+          a.og ? static_cast<const __nv_bfloat16*>(a.og) + grow * a.og_stride + h * kAtD + col0
+               : nullptr;
 #pragma unroll
-      for (int cc = 0; cc < kAtD / 32; ++cc) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + 2 * kAtBN + cc * 32, raw);
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t oe[32], oo[32];
+        tmem_ld32(tmem + lane_base + 2 * kAtBN + col0 + cc * 32, oe);
+        if (odd_written) tmem_ld32(tmem + lane_base + 3 * kAtBN + col0 + cc * 32, oo);
         tc_wait_ld();
         if (!row_ok) continue;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {  // merged, normalised output (in place)
+          float acc = __uint_as_float(oe[e]) * a_e;
+          if (odd_written) acc = fmaf(__uint_as_float(oo[e]), a_o, acc);
+          oe[e] = __float_as_uint(acc * inv_l);
+        }
+        const uint32_t* ov = oe;
         uint32_t packed[16];
         if (grow_p) {
           const uint4* gp = reinterpret_cast<const uint4*>(grow_p + cc * 32);
@@ -312,8 +365,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
               const int idx = qd * 8 + e;
-              const float o0 = bf16_round(__uint_as_float(raw[idx]) * inv_l);
-              const float o1 = bf16_round(__uint_as_float(raw[idx + 1]) * inv_l);
+              const float o0 = bf16_round(__uint_as_float(ov[idx]));
+              const float o1 = bf16_round(__uint_as_float(ov[idx + 1]));
               const float g0 = bf16_round(sigmoid_ref(__bfloat162float(ge[e])));
               const float g1 = bf16_round(sigmoid_ref(__bfloat162float(ge[e + 1])));
               packed[idx >> 1] = pack_bf16x2(o0 * g0, o1 * g1);
@@ -322,8 +375,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         } else {
 #pragma unroll
           for (int e = 0; e < 32; e += 2)
-            packed[e >> 1] = pack_bf16x2(__uint_as_float(raw[e]) * inv_l,
-                                         __uint_as_float(raw[e + 1]) * inv_l);
+            packed[e >> 1] = pack_bf16x2(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1]));
         }
         uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
@@ -336,7 +388,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kAtTmemCols);
   }

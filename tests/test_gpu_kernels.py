@@ -56,7 +56,8 @@ def test_rope_gates_matches_reference_rounding(dtype):
     # one bf16 ulp; for fp32 a few ulps (the float sigmoid itself differs by 1-2 ulps)
     ulp = vo.float().abs() * (2 ** -7 if dtype == torch.bfloat16 else 2 ** -20) + 1e-30
     assert bool((diff <= ulp).all())
-    assert (diff > 0).float().mean() < 0.02
+    if dtype == torch.bfloat16:
+        assert (diff > 0).float().mean() < 0.02  # rounding to bf16 hides most float ulps
 
 
 def test_rope_only_and_reference_signature():
