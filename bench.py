@@ -50,7 +50,7 @@ ATTN_TRAFFIC_NOTE = None
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg3")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -82,6 +82,12 @@ class ClockSampler:
         self.proc = None
         self.file = None
 
+    def _lines(self) -> int:
+        try:
+            return len(Path(self.file.name).read_text().splitlines())
+        except OSError:
+            return 0
+
     def __enter__(self):
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
@@ -89,12 +95,21 @@ class ClockSampler:
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
+            # the timed region starts once the sampler is producing samples
+            t0 = time.time()
+            while self._lines() < 1 and time.time() - t0 < 5.0:
+                time.sleep(0.05)
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # one more sample that covers the end of the timed region
+            n = self._lines()
+            t0 = time.time()
+            while self._lines() <= n and time.time() - t0 < 1.0:
+                time.sleep(0.05)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -288,7 +303,9 @@ def run_ours(args, cfg, rank: int, world: int, device):
             e2e_step()
         e2e_ev[i][1].record(stream)
     torch.cuda.synchronize()
-    e2e_local = sum(a.elapsed_time(b) for a, b in e2e_ev)
+    e2e_steps = [a.elapsed_time(b) for a, b in e2e_ev]
+    e2e_local = sum(e2e_steps)
+    e2e_median = statistics.median(e2e_steps)
     t = torch.tensor([e2e_local], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -340,7 +357,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
         "clocks": clocks.summary(),
         "e2e": {"value": round(cfg.B * cfg.T / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                "ms_per_step": round(e2e_ms, 4)},
+                "ms_per_step": round(e2e_ms, 4), "ms_per_step_median_rank0": round(e2e_median, 4)},
         "roofline": rl,
         "stage_ms": {k[2:]: round(v, 4) for k, v in stage_avg.items()},
         **extra,

@@ -6,7 +6,7 @@
 // ascending index sort of gsa_opt.py:674-677.  Ties are broken toward the
 // lower key index (torch.topk leaves tie order unspecified).
 //
-// One CTA (512 threads) per query row; n = min(q_pos0 + r + 1, Tkv) keys.
+// One CTA (256 threads) per query row; n = min(q_pos0 + r + 1, Tkv) keys.
 //  1. Stage the row as order-preserving uint32 keys (shared memory when the
 //     row fits, else re-read from global/L2) and reduce min/max of the finite
 //     keys and the finite count.
@@ -16,17 +16,18 @@
 //     digit would put every key in one bin).  After the first digit the keys
 //     of the threshold bin are compacted into a short candidate list and the
 //     remaining digits scan only that list.
-//  3. Emit: each warp owns a contiguous segment of the row; a counting phase
-//     and one scan of 16 warp totals give every warp its output offset, then
-//     it writes its selected columns in ascending order and one bitmask word
-//     per 32 keys straight from the ballot.  Keys equal to the threshold are
-//     taken lowest index first.
+//  3. Emit: each warp owns a contiguous segment of the row and writes one
+//     bitmask word per 32 keys straight from a ballot.  When column lists are
+//     requested, or only part of the keys equal to the threshold are taken
+//     (exact ties), a counting phase and a scan of the 8 warp totals first give
+//     every warp its output offset and its share of the tied keys (lowest
+//     index first); the bitmask-only forward path normally skips it.
 #include "kernels.h"
 
 namespace gsa {
 namespace {
 
-constexpr int kTopkThreads = 512;
+constexpr int kTopkThreads = 256;
 constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kBins = 2048;          // 11-bit digits
 constexpr int kDigitBits = 11;
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   if ((reinterpret_cast<uintptr_t>(srow) & 15u) == 0) {
     const float4* s4 = reinterpret_cast<const float4*>(srow);
     const int nv = n >> 2;
-    constexpr int U = 4;
+    constexpr int U = 8;
     for (int v0 = 0; v0 < nv; v0 += U * kTopkThreads) {
       float4 f[U];
 #pragma unroll
@@ -152,10 +153,13 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   uint32_t prefix = 0, pmask = 0;
   int krem = k_sel;
   bool fin_only = false;
+  bool eq_all = true;  // every key of the equal class is taken (no tie to split)
   if (n <= k_sel) {
     // everything is taken (prefix/pmask = 0: one class, krem >= n)
   } else if (nfin <= k_sel) {
-    // all finite keys, then the lowest-index -inf keys
+    // all finite keys, then the lowest-index -inf keys.  Those are listed with
+    // mask 0 but never set a bitmask bit, so only column lists rank them
+    // (need_rank below is then already forced by indices/mask).
     pmask = 0xFFFFFFFFu;
     prefix = kNegInfKey;
     krem = k_sel - nfin;
@@ -184,11 +188,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
         }
       }
       __syncthreads();
-      // suffix scan: thread t owns bins 4t..4t+3 counted from the top bin down
-      int own[4], loc = 0;
+      // suffix scan: thread t owns bins kBpt*t .. kBpt*t+kBpt-1 counted from the top bin down
+      constexpr int kBpt = kBins / kTopkThreads;
+      int own[kBpt], loc = 0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        own[q] = sh.hist[kBins - 1 - (4 * tid + q)];
+      for (int q = 0; q < kBpt; ++q) {
+        own[q] = sh.hist[kBins - 1 - (kBpt * tid + q)];
         loc += own[q];
       }
       int inc = loc;
@@ -204,9 +209,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
       if (before < krem && before + loc >= krem) {
         int cum = before;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < kBpt; ++q) {
           if (cum < krem && cum + own[q] >= krem) {
-            sh.sh_digit = kBins - 1 - (4 * tid + q);
+            sh.sh_digit = kBins - 1 - (kBpt * tid + q);
             sh.sh_above = cum;
             sh.sh_bin = own[q];
           }
@@ -219,7 +224,11 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
       const int bin_count = sh.sh_bin;
       prefix |= digit << shift;
       pmask |= dmask;
-      if (bin_count == krem || shift == 0) break;  // the whole class is taken / bits exhausted
+      if (bin_count == krem) break;                // the whole class is taken
+      if (shift == 0) {                            // bits exhausted: exact ties
+        eq_all = false;
+        break;
+      }
       // compact the class into the candidate list once it is short enough
       if (!use_cand && bin_count <= kCandCap) {
         if (tid == 0) sh.n_cand = 0;
@@ -245,51 +254,63 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   const int span = ((n + 31) / 32) * 32;
   const int seg = ((span / 32 + kTopkWarps - 1) / kTopkWarps) * 32;  // keys per warp
   const int s0 = min(warp * seg, span), s1 = min(s0 + seg, span);
-  auto classify = [&](int j, bool& gt, bool& eq) {
+  auto classify = [&](int j, bool& gt, bool& eq, bool& fin) {
     const bool valid = j < n;
-    const uint32_t u = valid ? key_at(j) : 0u;
-    const bool fin_ok = !fin_only || u != kNegInfKey;
+    const uint32_t u = valid ? key_at(j) : kNegInfKey;
+    fin = u != kNegInfKey;
+    const bool fin_ok = !fin_only || fin;
     const uint32_t m = u & pmask;
     gt = valid && fin_ok && m > prefix;
     eq = valid && fin_ok && m == prefix;
   };
-  int gt_w = 0, eq_w = 0;
-  for (int j0 = s0; j0 < s1; j0 += 32) {
-    bool gt, eq;
-    classify(j0 + lane, gt, eq);
-    gt_w += __popc(__ballot_sync(0xFFFFFFFFu, gt));
-    eq_w += __popc(__ballot_sync(0xFFFFFFFFu, eq));
-  }
-  if (lane == 0) {
-    sh.warp_a[warp] = gt_w;
-    sh.warp_b[warp] = eq_w;
-  }
-  __syncthreads();
-  int eq_before = 0, sel_before = 0;
-  for (int w = 0; w < warp; ++w) {
-    const int e = sh.warp_b[w];
-    sel_before += sh.warp_a[w] + max(0, min(krem - eq_before, e));
-    eq_before += e;
-  }
-  int eq_run = eq_before;
-  int out = sel_before;
-  for (int j0 = s0; j0 < s1; j0 += 32) {
-    const int j = j0 + lane;
-    bool gt, eq;
-    classify(j, gt, eq);
-    const uint32_t eqb = __ballot_sync(0xFFFFFFFFu, eq);
-    const bool sel = gt || (eq && eq_run + __popc(eqb & lt_mask) < krem);
-    eq_run += __popc(eqb);
-    const uint32_t selb = __ballot_sync(0xFFFFFFFFu, sel);
-    const bool live = sel && key_at(min(j, n - 1)) != kNegInfKey;
-    if (sel) {
-      const int pos = out + __popc(selb & lt_mask);
-      if (irow) irow[pos] = j;
-      if (mrow) mrow[pos] = live ? 1 : 0;
+  const bool need_rank = irow != nullptr || mrow != nullptr || !eq_all;
+  if (!need_rank) {
+    // bitmask only, whole equal class taken: one pass, no counting
+    for (int j0 = s0; j0 < s1; j0 += 32) {
+      bool gt, eq, fin;
+      classify(j0 + lane, gt, eq, fin);
+      const uint32_t liveb = __ballot_sync(0xFFFFFFFFu, (gt || eq) && fin);
+      if (lane == 0 && (j0 >> 5) < bm_words) brow[j0 >> 5] = liveb;
     }
-    const uint32_t liveb = __ballot_sync(0xFFFFFFFFu, live);
-    if (brow && lane == 0 && (j0 >> 5) < bm_words) brow[j0 >> 5] = liveb;
-    out += __popc(selb);
+  } else {
+    int gt_w = 0, eq_w = 0;
+    for (int j0 = s0; j0 < s1; j0 += 32) {
+      bool gt, eq, fin;
+      classify(j0 + lane, gt, eq, fin);
+      gt_w += __popc(__ballot_sync(0xFFFFFFFFu, gt));
+      eq_w += __popc(__ballot_sync(0xFFFFFFFFu, eq));
+    }
+    if (lane == 0) {
+      sh.warp_a[warp] = gt_w;
+      sh.warp_b[warp] = eq_w;
+    }
+    __syncthreads();
+    int eq_before = 0, sel_before = 0;
+    for (int w = 0; w < warp; ++w) {
+      const int e = sh.warp_b[w];
+      sel_before += sh.warp_a[w] + max(0, min(krem - eq_before, e));
+      eq_before += e;
+    }
+    int eq_run = eq_before;
+    int out = sel_before;
+    for (int j0 = s0; j0 < s1; j0 += 32) {
+      const int j = j0 + lane;
+      bool gt, eq, fin;
+      classify(j, gt, eq, fin);
+      const uint32_t eqb = __ballot_sync(0xFFFFFFFFu, eq);
+      const bool sel = gt || (eq && eq_run + __popc(eqb & lt_mask) < krem);
+      eq_run += __popc(eqb);
+      const uint32_t selb = __ballot_sync(0xFFFFFFFFu, sel);
+      const bool live = sel && fin;
+      if (sel) {
+        const int pos = out + __popc(selb & lt_mask);
+        if (irow) irow[pos] = j;
+        if (mrow) mrow[pos] = live ? 1 : 0;
+      }
+      const uint32_t liveb = __ballot_sync(0xFFFFFFFFu, live);
+      if (brow && lane == 0 && (j0 >> 5) < bm_words) brow[j0 >> 5] = liveb;
+      out += __popc(selb);
+    }
   }
   if (brow) {
     for (int64_t wd = span / 32 + tid; wd < bm_words; wd += kTopkThreads) brow[wd] = 0u;
