@@ -6,22 +6,26 @@
 // ascending index sort of gsa_opt.py:674-677.  Ties are broken toward the
 // lower key index (torch.topk leaves tie order unspecified).
 //
-// One CTA (256 threads) per query row; n = min(q_pos0 + r + 1, Tkv) keys.
-//  1. Stage the row as order-preserving uint32 keys (shared memory when the
-//     row fits, else re-read from global/L2) and reduce min/max of the finite
-//     keys and the finite count.
-//  2. Radix select of the k-th largest key, MSB first with 11-bit digits,
-//     starting at the highest bit in which the row's min and max keys differ
-//     (scores of one row share their top exponent bits, so a fixed first
-//     digit would put every key in one bin).  After the first digit the keys
-//     of the threshold bin are compacted into a short candidate list and the
-//     remaining digits scan only that list.
-//  3. Emit: each warp owns a contiguous segment of the row and writes one
-//     bitmask word per 32 keys straight from a ballot.  When column lists are
-//     requested, or only part of the keys equal to the threshold are taken
-//     (exact ties), a counting phase and a scan of the 8 warp totals first give
-//     every warp its output offset and its share of the tied keys (lowest
-//     index first); the bitmask-only forward path normally skips it.
+// One CTA of 256 threads per query row; the row has n = min(q_pos0 + r + 1,
+// Tkv) keys.  Scores become order-preserving uint32 keys (ord_key).
+//
+// Fast path (rows with n > k, the common case):
+//  1. 256 keys sampled evenly over the row give a key range [lo, hi], widened
+//     by a quarter on each side; bin(u) = clamp((u - lo) >> shift, 0, 2047)
+//     is monotonic in u.
+//  2. One read of the row builds the 2048-bin histogram of finite keys.
+//  3. The bin holding the k-th largest key is found by a suffix scan.
+//  4. A second read emits, per 32 keys, a ballot of the keys in higher bins
+//     into a shared-memory copy of the row's bitmask and collects the keys of
+//     the threshold bin into a candidate list.
+//  5. Candidates are ranked exactly by (key desc, index asc); the top ones are
+//     OR'd into the bitmask, which is then written out coalesced (and turned
+//     into an ascending column list when one is requested).
+// Rows the fast path cannot finish (n <= k, few finite scores, a degenerate
+// sample range or an over-full threshold bin — e.g. heavy exact ties) take the
+// exact path: an MSB-first 11-bit radix select starting at the highest bit in
+// which the row's min and max keys differ, with candidate compaction, and a
+// warp-segmented emit.  Both paths implement the same selection rule.
 #include "kernels.h"
 
 namespace gsa {
@@ -29,11 +33,10 @@ namespace {
 
 constexpr int kTopkThreads = 256;
 constexpr int kTopkWarps = kTopkThreads / 32;
-constexpr int kBins = 2048;          // 11-bit digits
+constexpr int kBins = 2048;   // 11-bit digits / histogram bins
 constexpr int kDigitBits = 11;
-constexpr int kCandCap = 1024;       // candidate list capacity
-// Rows up to this many keys are staged in shared memory (128 KB).
-constexpr int kTopkStageMax = 32768;
+constexpr int kCandCap = 1024;  // candidate list capacity
+constexpr int kMaxWords = 2048; // bitmask words held in shared memory (Tkv <= 65536)
 
 __device__ __forceinline__ uint32_t ord_key(float f) {
   const uint32_t x = __float_as_uint(f);
@@ -46,6 +49,7 @@ struct TopkShared {
   int hist[kBins];
   uint32_t cand_key[kCandCap];
   int cand_idx[kCandCap];
+  uint32_t bits[kMaxWords];
   int warp_a[kTopkWarps];
   int warp_b[kTopkWarps];
   uint32_t red_min[kTopkWarps];
@@ -55,12 +59,74 @@ struct TopkShared {
   int sh_digit, sh_above, sh_bin;
 };
 
-template <bool STAGED>
+// Block-wide reduction of (min, max, sum) into every thread.
+__device__ __forceinline__ void block_minmax_count(TopkShared& sh, uint32_t& kmin, uint32_t& kmax,
+                                                   int& cnt) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xFFFFFFFFu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xFFFFFFFFu, kmax, o));
+    cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+  }
+  if (lane == 0) {
+    sh.red_min[warp] = kmin;
+    sh.red_max[warp] = kmax;
+    sh.red_cnt[warp] = cnt;
+  }
+  __syncthreads();
+  kmin = 0xFFFFFFFFu;
+  kmax = 0u;
+  cnt = 0;
+#pragma unroll
+  for (int w = 0; w < kTopkWarps; ++w) {
+    kmin = min(kmin, sh.red_min[w]);
+    kmax = max(kmax, sh.red_max[w]);
+    cnt += sh.red_cnt[w];
+  }
+  __syncthreads();
+}
+
+// Suffix scan over sh.hist (bins counted from the top down): finds the bin
+// holding the krem-th largest key; sets sh_digit / sh_above / sh_bin.
+__device__ __forceinline__ void find_threshold_bin(TopkShared& sh, int krem) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kBpt = kBins / kTopkThreads;
+  int own[kBpt], loc = 0;
+#pragma unroll
+  for (int q = 0; q < kBpt; ++q) {
+    own[q] = sh.hist[kBins - 1 - (kBpt * tid + q)];
+    loc += own[q];
+  }
+  int inc = loc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) sh.warp_a[warp] = inc;
+  __syncthreads();
+  int before = inc - loc;
+  for (int w = 0; w < warp; ++w) before += sh.warp_a[w];
+  if (before < krem && before + loc >= krem) {
+    int cum = before;
+#pragma unroll
+    for (int q = 0; q < kBpt; ++q) {
+      if (cum < krem && cum + own[q] >= krem) {
+        sh.sh_digit = kBins - 1 - (kBpt * tid + q);
+        sh.sh_above = cum;
+        sh.sh_bin = own[q];
+      }
+      cum += own[q];
+    }
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0, int k_sel,
     int32_t* __restrict__ indices, uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask,
     int64_t bm_words) {
-  extern __shared__ uint32_t skeys[];
   __shared__ TopkShared sh;
 
   const int tid = threadIdx.x;
@@ -74,78 +140,170 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   int32_t* irow = indices ? indices + row * k_sel : nullptr;
   uint8_t* mrow = mask ? mask + row * k_sel : nullptr;
   uint32_t* brow = bitmask ? bitmask + row * bm_words : nullptr;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0;
+  const int nwords = (n + 31) / 32;
 
-  auto key_at = [&](int j) -> uint32_t {
-    if (STAGED) return skeys[j];
-    return ord_key(__ldg(srow + j));
-  };
+  auto key_at = [&](int j) -> uint32_t { return ord_key(__ldg(srow + j)); };
 
-  // ---- 1. stage + min/max/count of finite keys.  16-byte loads, four in
-  // flight per thread, when the row is 16-byte aligned; scalar otherwise.
+  // =================================================================== fast path
+  bool done = false;
+  if (n > k_sel && nwords <= kMaxWords) {
+    // 1. sample range
+    uint32_t smin = 0xFFFFFFFFu, smax = 0u;
+    int sfin = 0;
+    {
+      const int p = static_cast<int>((static_cast<int64_t>(tid) * (n - 1)) / (kTopkThreads - 1));
+      const uint32_t u = key_at(p);
+      if (u != kNegInfKey) {
+        smin = u;
+        smax = u;
+        sfin = 1;
+      }
+    }
+    for (int b = tid; b < kBins; b += kTopkThreads) sh.hist[b] = 0;
+    for (int w = tid; w < nwords; w += kTopkThreads) sh.bits[w] = 0u;
+    if (tid == 0) sh.n_cand = 0;
+    block_minmax_count(sh, smin, smax, sfin);
+    if (sfin > 0 && smax > smin) {
+      const uint32_t width = smax - smin;
+      const uint32_t margin = width >> 2;
+      const uint32_t lo = smin > margin ? smin - margin : 0u;
+      const uint32_t span_w = min(0xFFFFFFFFu - lo, width + 2 * margin);
+      const int shift = max(0, 32 - __clz(span_w) - kDigitBits);
+      auto bin_of = [&](uint32_t u) -> int {
+        return u <= lo ? 0 : min(static_cast<int>((u - lo) >> shift), kBins - 1);
+      };
+      // 2. histogram of finite keys
+      int nfin = 0;
+      auto hist_key = [&](float f) {
+        const uint32_t u = ord_key(f);
+        if (u != kNegInfKey) {
+          ++nfin;
+          atomicAdd(&sh.hist[bin_of(u)], 1);
+        }
+      };
+      int jv = 0;
+      if (vec_ok) {
+        const float4* s4 = reinterpret_cast<const float4*>(srow);
+        const int nv = n >> 2;
+        constexpr int U = 4;
+        for (int v0 = 0; v0 < nv; v0 += U * kTopkThreads) {
+          float4 f[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int v = v0 + u * kTopkThreads + tid;
+            f[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if (v0 + u * kTopkThreads + tid < nv) {
+              hist_key(f[u].x);
+              hist_key(f[u].y);
+              hist_key(f[u].z);
+              hist_key(f[u].w);
+            }
+          }
+        }
+        jv = nv << 2;
+      }
+      for (int j = jv + tid; j < n; j += kTopkThreads) hist_key(__ldg(srow + j));
+      uint32_t d0 = 0, d1 = 0;
+      block_minmax_count(sh, d0, d1, nfin);  // (syncs, so the histogram is complete)
+      if (nfin > k_sel) {
+        // 3. threshold bin
+        find_threshold_bin(sh, k_sel);
+        const int bstar = sh.sh_digit;
+        const int krem = k_sel - sh.sh_above;
+        const int bcount = sh.sh_bin;
+        if (bcount <= kCandCap) {
+          // 4. bits for higher bins, candidates of the threshold bin
+          const int seg = ((nwords + kTopkWarps - 1) / kTopkWarps) * 32;
+          const int s0 = min(warp * seg, nwords * 32), s1 = min(s0 + seg, nwords * 32);
+          for (int j0 = s0; j0 < s1; j0 += 32) {
+            const int j = j0 + lane;
+            const uint32_t u = j < n ? key_at(j) : kNegInfKey;
+            const bool fin = u != kNegInfKey;
+            const int bn = fin ? bin_of(u) : -1;
+            const uint32_t hib = __ballot_sync(0xFFFFFFFFu, bn > bstar);
+            if (bn == bstar) {
+              const int c = atomicAdd(&sh.n_cand, 1);
+              sh.cand_key[c] = u;
+              sh.cand_idx[c] = j;
+            }
+            if (lane == 0) sh.bits[j0 >> 5] = hib;
+          }
+          __syncthreads();
+          // 5. exact rank among the candidates: (key desc, index asc)
+          const int nc = sh.n_cand;
+          for (int c = tid; c < nc; c += kTopkThreads) {
+            const uint32_t u = sh.cand_key[c];
+            const int ji = sh.cand_idx[c];
+            int rank = 0;
+            for (int o = 0; o < nc; ++o) {
+              const uint32_t uo = sh.cand_key[o];
+              rank += (uo > u || (uo == u && sh.cand_idx[o] < ji)) ? 1 : 0;
+            }
+            if (rank < krem) atomicOr(&sh.bits[ji >> 5], 1u << (ji & 31));
+          }
+          __syncthreads();
+          if (brow) {
+            for (int64_t w = tid; w < bm_words; w += kTopkThreads)
+              brow[w] = w < nwords ? sh.bits[w] : 0u;
+          }
+          if (irow || mrow) {
+            // ascending column list from the bitmask; every pick is finite
+            const int wseg = (nwords + kTopkWarps - 1) / kTopkWarps;
+            const int w0 = min(warp * wseg, nwords), w1 = min(w0 + wseg, nwords);
+            int cnt = 0;
+            for (int w = w0 + lane; w < w1; w += 32) cnt += __popc(sh.bits[w]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+            if (lane == 0) sh.warp_a[warp] = cnt;
+            __syncthreads();
+            int out = 0;
+            for (int w = 0; w < warp; ++w) out += sh.warp_a[w];
+            for (int wb = w0; wb < w1; wb += 32) {
+              const int w = wb + lane;
+              const uint32_t word = w < w1 ? sh.bits[w] : 0u;
+              const int pc = __popc(word);
+              int incl = pc;
+#pragma unroll
+              for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl += y;
+              }
+              int pos = out + incl - pc;
+              uint32_t rest = word;
+              while (rest) {
+                const int bit = __ffs(rest) - 1;
+                rest &= rest - 1;
+                if (irow) irow[pos] = w * 32 + bit;
+                if (mrow) mrow[pos] = 1;
+                ++pos;
+              }
+              out += __shfl_sync(0xFFFFFFFFu, incl, 31);
+            }
+          }
+          done = true;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (done) return;
+
+  // =================================================================== exact path
   uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
   int nfin = 0;
-  auto note = [&](uint32_t u) {
+  for (int j = tid; j < n; j += kTopkThreads) {
+    const uint32_t u = key_at(j);
     if (u != kNegInfKey) {
       kmin = min(kmin, u);
       kmax = max(kmax, u);
       ++nfin;
     }
-  };
-  auto take = [&](int j, float f) {
-    const uint32_t u = ord_key(f);
-    if (STAGED) skeys[j] = u;
-    note(u);
-  };
-  int j_vec = 0;
-  if ((reinterpret_cast<uintptr_t>(srow) & 15u) == 0) {
-    const float4* s4 = reinterpret_cast<const float4*>(srow);
-    const int nv = n >> 2;
-    constexpr int U = 8;
-    for (int v0 = 0; v0 < nv; v0 += U * kTopkThreads) {
-      float4 f[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int v = v0 + u * kTopkThreads + tid;
-        f[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int v = v0 + u * kTopkThreads + tid;
-        if (v < nv) {
-          const uint4 k4 = make_uint4(ord_key(f[u].x), ord_key(f[u].y), ord_key(f[u].z),
-                                      ord_key(f[u].w));
-          if (STAGED) reinterpret_cast<uint4*>(skeys)[v] = k4;  // one 16-byte store
-          note(k4.x);
-          note(k4.y);
-          note(k4.z);
-          note(k4.w);
-        }
-      }
-    }
-    j_vec = nv << 2;
   }
-  for (int j = j_vec + tid; j < n; j += kTopkThreads) take(j, __ldg(srow + j));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    kmin = min(kmin, __shfl_xor_sync(0xFFFFFFFFu, kmin, o));
-    kmax = max(kmax, __shfl_xor_sync(0xFFFFFFFFu, kmax, o));
-    nfin += __shfl_xor_sync(0xFFFFFFFFu, nfin, o);
-  }
-  if (lane == 0) {
-    sh.red_min[warp] = kmin;
-    sh.red_max[warp] = kmax;
-    sh.red_cnt[warp] = nfin;
-  }
-  __syncthreads();
-  kmin = 0xFFFFFFFFu;
-  kmax = 0u;
-  nfin = 0;
-#pragma unroll
-  for (int w = 0; w < kTopkWarps; ++w) {
-    kmin = min(kmin, sh.red_min[w]);
-    kmax = max(kmax, sh.red_max[w]);
-    nfin += sh.red_cnt[w];
-  }
+  block_minmax_count(sh, kmin, kmax, nfin);
 
   // Selection = keys in a class above `prefix` (under `pmask`), plus the
   // first `krem` keys (by index) of the class equal to `prefix`.  `fin_only`
@@ -166,7 +324,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   } else {
     fin_only = true;
     const uint32_t diff = kmin ^ kmax;
-    int hb = diff ? 31 - __clz(diff) : 0;      // highest differing bit
+    int hb = diff ? 31 - __clz(diff) : 0;  // highest differing bit
     pmask = hb >= 31 ? 0u : ~((2u << hb) - 1u);
     prefix = kmin & pmask;
     int shift = max(hb - (kDigitBits - 1), 0);
@@ -188,44 +346,14 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
         }
       }
       __syncthreads();
-      // suffix scan: thread t owns bins kBpt*t .. kBpt*t+kBpt-1 counted from the top bin down
-      constexpr int kBpt = kBins / kTopkThreads;
-      int own[kBpt], loc = 0;
-#pragma unroll
-      for (int q = 0; q < kBpt; ++q) {
-        own[q] = sh.hist[kBins - 1 - (kBpt * tid + q)];
-        loc += own[q];
-      }
-      int inc = loc;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-        if (lane >= o) inc += y;
-      }
-      if (lane == 31) sh.warp_a[warp] = inc;
-      __syncthreads();
-      int before = inc - loc;
-      for (int w = 0; w < warp; ++w) before += sh.warp_a[w];
-      if (before < krem && before + loc >= krem) {
-        int cum = before;
-#pragma unroll
-        for (int q = 0; q < kBpt; ++q) {
-          if (cum < krem && cum + own[q] >= krem) {
-            sh.sh_digit = kBins - 1 - (kBpt * tid + q);
-            sh.sh_above = cum;
-            sh.sh_bin = own[q];
-          }
-          cum += own[q];
-        }
-      }
-      __syncthreads();
+      find_threshold_bin(sh, krem);
       const uint32_t digit = static_cast<uint32_t>(sh.sh_digit);
       krem -= sh.sh_above;
       const int bin_count = sh.sh_bin;
       prefix |= digit << shift;
       pmask |= dmask;
-      if (bin_count == krem) break;                // the whole class is taken
-      if (shift == 0) {                            // bits exhausted: exact ties
+      if (bin_count == krem) break;  // the whole class is taken
+      if (shift == 0) {              // bits exhausted: exact ties
         eq_all = false;
         break;
       }
@@ -250,8 +378,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     __syncthreads();
   }
 
-  // ---- 3. emit in ascending index order (warp-contiguous segments)
-  const int span = ((n + 31) / 32) * 32;
+  // ---- emit in ascending index order (warp-contiguous segments)
+  const int span = nwords * 32;
   const int seg = ((span / 32 + kTopkWarps - 1) / kTopkWarps) * 32;  // keys per warp
   const int s0 = min(warp * seg, span), s1 = min(s0 + seg, span);
   auto classify = [&](int j, bool& gt, bool& eq, bool& fin) {
@@ -270,7 +398,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
       bool gt, eq, fin;
       classify(j0 + lane, gt, eq, fin);
       const uint32_t liveb = __ballot_sync(0xFFFFFFFFu, (gt || eq) && fin);
-      if (lane == 0 && (j0 >> 5) < bm_words) brow[j0 >> 5] = liveb;
+      if (brow && lane == 0 && (j0 >> 5) < bm_words) brow[j0 >> 5] = liveb;
     }
   } else {
     int gt_w = 0, eq_w = 0;
@@ -330,25 +458,8 @@ cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq
                         int64_t bitmask_words, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * Tq;
   if (rows == 0) return cudaSuccess;
-  const int max_n = min(q_pos0 + Tq, Tkv);
-  if (max_n <= kTopkStageMax) {
-    const size_t smem = static_cast<size_t>(max(max_n, 1)) * sizeof(uint32_t);
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(topk_kernel<true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kTopkStageMax * static_cast<int>(sizeof(uint32_t)));
-      if (e != cudaSuccess) return e;
-      attr_set[dev] = true;
-    }
-    topk_kernel<true><<<static_cast<unsigned>(rows), kTopkThreads, smem, stream>>>(
-        scores, score_stride, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask, bitmask_words);
-  } else {
-    topk_kernel<false><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-        scores, score_stride, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask, bitmask_words);
-  }
+  topk_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+      scores, score_stride, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask, bitmask_words);
   return cudaGetLastError();
 }
 
