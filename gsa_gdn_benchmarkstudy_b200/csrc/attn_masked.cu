@@ -52,7 +52,7 @@ constexpr int kAtTileBytes = kAtBM * kAtD * 2;  // 32 KB: two 128x64 swizzled bo
 constexpr int kAtBoxBytes = kAtTileBytes / 2;   // 16 KB
 constexpr int kAtThreads = 320;
 constexpr int kAtTmemCols = 512;
-constexpr float kRescaleLog2 = 8.0f;            // p may reach 2^8 before m is raised
+constexpr float kRescaleP = 256.0f;             // p may reach 2^8 before m is raised
 
 struct AtSmem {
   uint64_t q_full;
@@ -76,6 +76,98 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
                "r"(d)
                : "memory");
+}
+
+// Masked max of this thread's row of one S tile (raw dot-product units).
+__device__ __forceinline__ float row_tile_max(uint32_t s_taddr, const uint32_t (&wb)[4]) {
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+  for (int cc = 0; cc < 4; ++cc) {
+    uint32_t sv[32];
+    tmem_ld32(s_taddr + cc * 32, sv);
+    tc_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if ((wb[cc] >> e) & 1u) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sv[e]));
+  }
+  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// One pass over this thread's row of an S tile: p = 2^(s*c - m*c) for the
+// selected keys (0 elsewhere) goes, as bf16, into row i of the swizzled P
+// tile at pb.  Returns the row sum of p; `over` is set when some p exceeds
+// kRescaleP (the running max m must then be raised).
+__device__ __forceinline__ float row_exp_pass(uint32_t s_taddr, const uint32_t (&wb)[4], float c,
+                                              float m, uint32_t pb, int i, bool& over) {
+  const float mc = (m == -INFINITY) ? 0.f : m * c;
+  const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
+  uint64_t l2a = 0, l2b = 0;  // packed partial row sums
+  uint32_t pmax = 0;          // packed bf16 max of p (p >= 0)
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    uint32_t sv[32];
+    tmem_ld32(s_taddr + cc * 32, sv);
+    tc_wait_ld();
+    uint32_t packed[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      const uint64_t x2 =
+          f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2, nmc2);
+      const float p0 = ((wb[cc] >> e) & 1u) ? fast_ex2(f2_lo(x2)) : 0.f;
+      const float p1 = ((wb[cc] >> (e + 1)) & 1u) ? fast_ex2(f2_hi(x2)) : 0.f;
+      if (e & 2) l2b = f2_add(l2b, f2_pack(p0, p1));
+      else l2a = f2_add(l2a, f2_pack(p0, p1));
+      packed[e >> 1] = pack_bf16x2(p0, p1);
+      pmax = bf2_max(pmax, packed[e >> 1]);
+    }
+    // keys 32cc..32cc+31 -> box cc/2, 16-byte chunks 4*(cc%2) .. +3 of row i
+    const uint32_t box = pb + (cc >> 1) * kAtBoxBytes;
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd)
+      st_shared_v4(box + sw128_offset(i, (cc & 1) * 4 + qd), packed[4 * qd], packed[4 * qd + 1],
+                   packed[4 * qd + 2], packed[4 * qd + 3]);
+  }
+  const float pm = fmaxf(__uint_as_float(pmax << 16), __uint_as_float(pmax & 0xFFFF0000u));
+  over = pm > kRescaleP;
+  const uint64_t l2 = f2_add(l2a, l2b);
+  return f2_lo(l2) + f2_hi(l2);
+}
+
+struct RowState {
+  float m, l, lt;
+};
+
+// Rare path, kept out of line so the hot loop is not duplicated: rows whose p
+// overshot raise m to the exact tile max; l and this warp's O rows (earlier
+// tiles of the same parity) are scaled by 2^((m_old - m_new) c); then the
+// tile's p are recomputed.  All lanes of the warp call it together.
+__device__ __noinline__ RowState row_rescale_redo(uint32_t s_taddr, uint32_t o_taddr, uint32_t w0,
+                                                  uint32_t w1, uint32_t w2, uint32_t w3, float c,
+                                                  float m, float l, bool over, int j,
+                                                  uint32_t pb, int i) {
+  const uint32_t wb[4] = {w0, w1, w2, w3};
+  const float tm = row_tile_max(s_taddr, wb);
+  float alpha = 1.f;
+  if (over) {
+    alpha = fast_ex2((m - tm) * c);
+    m = tm;
+  }
+  l *= alpha;
+  if (j >= 2) {  // O of this parity holds P.V of earlier tiles
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t ov[32];
+      tmem_ld32(o_taddr + cc * 32, ov);
+      tc_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+      tmem_st32(o_taddr + cc * 32, ov);
+    }
+    tc_wait_st();
+  }
+  bool over2;
+  const float lt = row_exp_pass(s_taddr, wb, c, m, pb, i, over2);
+  return RowState{m, l, lt};
 }
 
 __global__ void __launch_bounds__(kAtThreads, 1)
@@ -233,82 +325,21 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const uint32_t wb[4] = {bits.x, bits.y, bits.z, bits.w};
       if (!(ok = mbar_wait_warp(&sh->s_full[par], ph, a.err, abort))) break;
       tc_fence_after();
-      // a row's first selected keys: take the exact tile max to start m
+      // a row's first selected keys: start m from the exact tile max
       if (__any_sync(0xFFFFFFFFu, row_ok && m == -INFINITY)) {
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t sv[32];
-          tmem_ld32(s_taddr + cc * 32, sv);
-          tc_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if ((wb[cc] >> e) & 1u) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sv[e]));
-        }
-        if (m == -INFINITY) m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        const float tm = row_tile_max(s_taddr, wb);
+        if (m == -INFINITY) m = tm;
       }
       // P buffer par is free (and O_par stable) once P.V of tile j-2 finished
       if (!(ok = mbar_wait_warp(&sh->p_empty[par], ph ^ 1, a.err, abort))) break;
-
-      // p = 2^(s*c - m*c) with the running max; returns this tile's row sum
-      // and the largest exponent s*c - m*c among selected keys
-      auto exp_pass = [&](float& amax) -> float {
-        const float mc = (m == -INFINITY) ? 0.f : m * c;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
-        float a4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t sv[32];
-          tmem_ld32(s_taddr + cc * 32, sv);
-          tc_wait_ld();
-          uint32_t packed[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float p0 = 0.f, p1 = 0.f;
-            if ((wb[cc] >> e) & 1u) {
-              const float x = fmaf(__uint_as_float(sv[e]), c, -mc);
-              a4[e & 3] = fmaxf(a4[e & 3], x);
-              p0 = fast_ex2(x);
-            }
-            if ((wb[cc] >> (e + 1)) & 1u) {
-              const float x = fmaf(__uint_as_float(sv[e + 1]), c, -mc);
-              a4[(e + 1) & 3] = fmaxf(a4[(e + 1) & 3], x);
-              p1 = fast_ex2(x);
-            }
-            l4[(e >> 1) & 3] += p0 + p1;
-            packed[e >> 1] = pack_bf16x2(p0, p1);
-          }
-          // keys 32cc..32cc+31 -> box cc/2, 16-byte chunks 4*(cc%2) .. +3 of row i
-          const uint32_t box = pb + (cc >> 1) * kAtBoxBytes;
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd)
-            st_shared_v4(box + sw128_offset(i, (cc & 1) * 4 + qd), packed[4 * qd],
-                         packed[4 * qd + 1], packed[4 * qd + 2], packed[4 * qd + 3]);
-        }
-        amax = fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3]));
-        return (l4[0] + l4[1]) + (l4[2] + l4[3]);
-      };
-      float amax;
-      float lt = exp_pass(amax);
-      // rows whose p overshot 2^8: raise m to the tile max, rescale, redo the tile
-      const bool over = amax > kRescaleLog2;
+      bool over;
+      float lt = row_exp_pass(s_taddr, wb, c, m, pb, i, over);
       if (__any_sync(0xFFFFFFFFu, over)) {
-        const float alpha = over ? fast_ex2(-amax) : 1.f;  // 2^((m_old - m_new) c)
-        if (over) m += amax / c;
-        l *= alpha;
-        if (j >= 2) {  // O_par holds P.V of earlier tiles of this parity
-#pragma unroll 1
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t ov[32];
-            tmem_ld32(o_taddr + cc * 32, ov);
-            tc_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st32(o_taddr + cc * 32, ov);
-          }
-          tc_wait_st();
-        }
-        lt = exp_pass(amax);
+        const RowState rs =
+            row_rescale_redo(s_taddr, o_taddr, wb[0], wb[1], wb[2], wb[3], c, m, l, over, j, pb, i);
+        m = rs.m;
+        l = rs.l;
+        lt = rs.lt;
       }
       l += lt;
       fence_proxy_async_smem();
