@@ -280,10 +280,13 @@ def run_ours(args, cfg, rank: int, world: int, device):
 
     # per-kernel averages over the timed region (events on the launch stream)
     stage_ms: dict = {}
-    for name, a, b in stage_events:
+    own_launches = 0
+    for name, a, b, n_launch in stage_events:
         stage_ms.setdefault(name, []).append(a.elapsed_time(b))
+        if name.startswith("k:"):
+            own_launches += n_launch
     stage_avg = {k: sum(v) / len(v) for k, v in stage_ms.items()}
-    launches_per_step = sum(len(v) for k, v in stage_ms.items() if k.startswith("k:")) / args.steps
+    split = time_indexer_and_topk(model, x_dev if world == 1 else None, cfg)
 
     # ---------------- end-to-end through the public API, host buffers
     out_host = torch.empty(cfg.B, cfg.T, cfg.D, dtype=cfg.torch_dtype).pin_memory()
@@ -319,7 +322,6 @@ def run_ours(args, cfg, rank: int, world: int, device):
     pk = peaks()
     wm = WorkModel(cfg)
     attn_ms = stage_avg.get("k:masked_attention")
-    idx_ms = stage_avg.get("k:indexer")
     rl = None
     if attn_ms:
         # algorithmic work of one launch: QK^T + PV over the causal key range of the
@@ -334,9 +336,10 @@ def run_ours(args, cfg, rank: int, world: int, device):
         if ATTN_TRAFFIC_NOTE:
             rl["traffic_note"] = ATTN_TRAFFIC_NOTE
     extra = {}
-    if idx_ms:
-        n_idx = stage_count(stage_ms, "k:indexer", args.steps)
-        extra["indexer_tflops"] = round(wm.indexer_flops / world / n_idx / (idx_ms / 1e3) / 1e12, 2)
+    if split:
+        extra["indexer_ms"] = round(split["indexer"], 4)
+        extra["topk_ms"] = round(split["topk"], 4)
+        extra["indexer_tflops"] = round(wm.indexer_flops / (split["indexer"] / 1e3) / 1e12, 2)
     if attn_ms:
         n_at = stage_count(stage_ms, "k:masked_attention", args.steps)
         extra["sparse_attn_gather_equiv_gbs"] = round(
@@ -353,7 +356,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
                    "parallelism": ("single GPU" if world == 1 else
                                    ("query-row zig-zag shards" if cfg.B == 1 else "batch shards")),
                    "l2": "flushed between steps (256 MB memset outside the step events)"},
-        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "gpu_launches": own_launches,
         "clocks": clocks.summary(),
         "e2e": {"value": round(cfg.B * cfg.T / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
@@ -365,6 +368,36 @@ def run_ours(args, cfg, rank: int, world: int, device):
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_sample_rows, os.cpu_count() or 1)
     print(json.dumps(line), flush=True)
+
+
+def time_indexer_and_topk(model, x, cfg, iters: int = 5):
+    """Event-timed indexer and top-k kernels alone (the forward runs them fused
+    in one C call), on this step's own projections; single-GPU runs only."""
+    if x is None:
+        return None
+    from gsa_gdn_benchmarkstudy_b200 import ops
+
+    parts = model.split(model.project(x))
+    ix = model.indexer
+    k_eff = model.topk_selector.k_effective(cfg.T)
+    res = {}
+    scores = ops.indexer_scores(parts["iq"], parts["ik"], parts["iw"], ix.idx_bias, ix.scale,
+                                fill_upper=False)
+    for name in ("indexer", "topk"):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            if name == "indexer":
+                ops.indexer_scores(parts["iq"], parts["ik"], parts["iw"], ix.idx_bias, ix.scale,
+                                   fill_upper=False, out=scores.as_strided(
+                                       (cfg.B, cfg.T, scores.stride(1)),
+                                       (scores.stride(0), scores.stride(1), 1)))
+            else:
+                ops.topk_select(scores, k_eff, want_indices=False, want_mask=False)
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / iters
+    return res
 
 
 def stage_count(stage_ms: dict, name: str, steps: int) -> float:

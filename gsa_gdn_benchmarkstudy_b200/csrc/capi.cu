@@ -110,6 +110,75 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int finish(cudaError_t e) { return e == cudaSuccess ? GSA_OK : set_cuda_error(e); }
 
+int indexer_impl(const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* w,
+                 int64_t w_stride, const float* bias, float scale, int dtype, int B, int Tq,
+                 int Tkv, int q_pos0, int H_I, int d_I, float* out, int64_t out_stride,
+                 int fill_upper, cudaStream_t s) {
+  if (dtype != GSA_DTYPE_BF16 && dtype != GSA_DTYPE_F32)
+    return set_error(GSA_ERR_UNSUPPORTED, "dtype must be bf16 or f32");
+  if (B < 0 || Tq < 0 || Tkv < 0 || q_pos0 < 0 || H_I <= 0 || d_I <= 0)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (B == 0 || Tq == 0 || Tkv == 0) return GSA_OK;
+  if (!q || !k || !w || !bias || !out) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  if (out_stride < Tkv) return set_error(GSA_ERR_INVALID_ARG, "out_stride < Tkv");
+  if (q_stride < static_cast<int64_t>(H_I) * d_I || k_stride < d_I || w_stride < H_I)
+    return set_error(GSA_ERR_INVALID_ARG, "row stride smaller than the row");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  if (fill_upper) {
+    cudaError_t e = gsa::launch_fill_upper(out, out_stride, B, Tq, Tkv, q_pos0, s);
+    if (e != cudaSuccess) return set_cuda_error(e);
+  }
+  if (dtype == GSA_DTYPE_BF16 && H_I == 4 && d_I == 64) {
+    if (!aligned16(q) || !aligned16(k) || (q_stride * 2) % 16 || (k_stride * 2) % 16 ||
+        !aligned16(out) || (out_stride * 4) % 16)
+      return set_error(GSA_ERR_ALIGNMENT, "indexer rows must be 16-byte aligned");
+    CUtensorMap qmap, kmap;
+    rc = make_map_bf16_3d(&qmap, q, static_cast<uint64_t>(H_I) * d_I, Tq, B, q_stride * 2,
+                          static_cast<uint64_t>(Tq) * q_stride * 2, 128);
+    if (rc) return rc;
+    rc = make_map_bf16_3d(&kmap, k, d_I, Tkv, B, k_stride * 2,
+                          static_cast<uint64_t>(Tkv) * k_stride * 2, 32);
+    if (rc) return rc;
+    gsa::IndexerArgs a;
+    a.w = w;
+    a.w_stride = w_stride;
+    a.bias = bias;
+    a.scale = scale;
+    a.B = B;
+    a.Tq = Tq;
+    a.Tkv = Tkv;
+    a.q_pos0 = q_pos0;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.err = st->err;
+    return finish(gsa::launch_indexer_tc(qmap, kmap, a, s));
+  }
+  if (H_I > 8 || d_I > 128 || H_I * d_I > 512)
+    return set_error(GSA_ERR_UNSUPPORTED, "indexer heads/dims beyond the CUDA-core kernel");
+  return finish(gsa::launch_indexer_simt(q, q_stride, k, k_stride, w, w_stride, bias, scale,
+                                         dtype, B, Tq, Tkv, q_pos0, H_I, d_I, out, out_stride,
+                                         s));
+}
+
+
+// Row stride (floats) of the score rows gsa_indexer_topk keeps in its workspace.
+int64_t score_row_stride(int Tkv) { return (static_cast<int64_t>(Tkv) + 3) / 4 * 4; }
+
+int indexer_topk_impl(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                      const void* w, int64_t w_stride, const float* bias, float scale, int dtype,
+                      int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I, int k_sel,
+                      float* scores, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                      int64_t bitmask_words, cudaStream_t s) {
+  const int64_t stride = score_row_stride(Tkv);
+  int rc = indexer_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
+                        q_pos0, H_I, d_I, scores, stride, 0, s);
+  if (rc) return rc;
+  return finish(gsa::launch_topk(scores, stride, B, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
+                                 bitmask_words, s));
+}
+
 }  // namespace
 
 extern "C" {
@@ -183,53 +252,32 @@ int gsa_indexer_scores(const void* q, int64_t q_stride, const void* k, int64_t k
                        const void* w, int64_t w_stride, const float* bias, float scale, int dtype,
                        int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I, float* out,
                        int64_t out_stride, int fill_upper, void* stream) {
-  if (dtype != GSA_DTYPE_BF16 && dtype != GSA_DTYPE_F32)
-    return set_error(GSA_ERR_UNSUPPORTED, "dtype must be bf16 or f32");
-  if (B < 0 || Tq < 0 || Tkv < 0 || q_pos0 < 0 || H_I <= 0 || d_I <= 0)
-    return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
-  if (B == 0 || Tq == 0 || Tkv == 0) return GSA_OK;
-  if (!q || !k || !w || !bias || !out) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
-  if (out_stride < Tkv) return set_error(GSA_ERR_INVALID_ARG, "out_stride < Tkv");
-  if (q_stride < static_cast<int64_t>(H_I) * d_I || k_stride < d_I || w_stride < H_I)
-    return set_error(GSA_ERR_INVALID_ARG, "row stride smaller than the row");
-  DeviceState* st = nullptr;
-  int rc = device_state(&st);
-  if (rc) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (fill_upper) {
-    cudaError_t e = gsa::launch_fill_upper(out, out_stride, B, Tq, Tkv, q_pos0, s);
-    if (e != cudaSuccess) return set_cuda_error(e);
-  }
-  if (dtype == GSA_DTYPE_BF16 && H_I == 4 && d_I == 64) {
-    if (!aligned16(q) || !aligned16(k) || (q_stride * 2) % 16 || (k_stride * 2) % 16 ||
-        !aligned16(out) || (out_stride * 4) % 16)
-      return set_error(GSA_ERR_ALIGNMENT, "indexer rows must be 16-byte aligned");
-    CUtensorMap qmap, kmap;
-    rc = make_map_bf16_3d(&qmap, q, static_cast<uint64_t>(H_I) * d_I, Tq, B, q_stride * 2,
-                          static_cast<uint64_t>(Tq) * q_stride * 2, 128);
-    if (rc) return rc;
-    rc = make_map_bf16_3d(&kmap, k, d_I, Tkv, B, k_stride * 2,
-                          static_cast<uint64_t>(Tkv) * k_stride * 2, 32);
-    if (rc) return rc;
-    gsa::IndexerArgs a;
-    a.w = w;
-    a.w_stride = w_stride;
-    a.bias = bias;
-    a.scale = scale;
-    a.B = B;
-    a.Tq = Tq;
-    a.Tkv = Tkv;
-    a.q_pos0 = q_pos0;
-    a.out = out;
-    a.out_stride = out_stride;
-    a.err = st->err;
-    return finish(gsa::launch_indexer_tc(qmap, kmap, a, s));
-  }
-  if (H_I > 8 || d_I > 128 || H_I * d_I > 512)
-    return set_error(GSA_ERR_UNSUPPORTED, "indexer heads/dims beyond the CUDA-core kernel");
-  return finish(gsa::launch_indexer_simt(q, q_stride, k, k_stride, w, w_stride, bias, scale,
-                                         dtype, B, Tq, Tkv, q_pos0, H_I, d_I, out, out_stride,
-                                         s));
+  return indexer_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
+                      q_pos0, H_I, d_I, out, out_stride, fill_upper,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int64_t gsa_indexer_topk_workspace_size(int B, int Tq, int Tkv) {
+  if (B <= 0 || Tq <= 0 || Tkv <= 0) return 0;
+  return static_cast<int64_t>(B) * Tq * score_row_stride(Tkv) * static_cast<int64_t>(sizeof(float));
+}
+
+int gsa_indexer_topk(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                     const void* w, int64_t w_stride, const float* bias, float scale, int dtype,
+                     int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I, int k_sel,
+                     void* workspace, int64_t workspace_bytes, int32_t* indices, uint8_t* mask,
+                     uint32_t* bitmask, int64_t bitmask_words, void* stream) {
+  if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0 || k_sel <= 0 || k_sel > Tkv)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes (need 0 < k_sel <= Tkv)");
+  if (B == 0 || Tq == 0) return GSA_OK;
+  if (!workspace) return set_error(GSA_ERR_INVALID_ARG, "workspace is NULL");
+  if (workspace_bytes < gsa_indexer_topk_workspace_size(B, Tq, Tkv))
+    return set_error(GSA_ERR_INVALID_ARG, "workspace smaller than gsa_indexer_topk_workspace_size");
+  if (bitmask && bitmask_words < gsa_bitmask_words(Tkv))
+    return set_error(GSA_ERR_INVALID_ARG, "bitmask_words < gsa_bitmask_words(Tkv)");
+  return indexer_topk_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
+                           q_pos0, H_I, d_I, k_sel, static_cast<float*>(workspace), indices, mask,
+                           bitmask, bitmask_words, static_cast<cudaStream_t>(stream));
 }
 
 int gsa_topk_select(const float* scores, int64_t score_stride, int B, int Tq, int Tkv, int q_pos0,

@@ -48,10 +48,11 @@ class _Stage:
     also records a CUDA event pair on the current stream (used by bench.py to
     time each kernel inside the timed region)."""
 
-    __slots__ = ("mod", "name", "nvtx", "a")
+    __slots__ = ("mod", "name", "nvtx", "a", "launches")
 
-    def __init__(self, mod, name: str, nvtx: str):
+    def __init__(self, mod, name: str, nvtx: str, launches: int = 1):
         self.mod, self.name, self.nvtx, self.a = mod, name, nvtx, None
+        self.launches = launches  # kernels this stage launches
 
     def __enter__(self):
         _nvtx_push(self.nvtx)
@@ -64,7 +65,7 @@ class _Stage:
         if self.a is not None:
             b = torch.cuda.Event(enable_timing=True)
             b.record()
-            self.mod._stage_events.append((self.name, self.a, b))
+            self.mod._stage_events.append((self.name, self.a, b, self.launches))
         _nvtx_pop()
         return False
 
@@ -309,20 +310,17 @@ class GatedSparseAttention(nn.Module):
         Tkv = k_all.shape[1]
         H = self.num_heads
         k_eff = self.topk_selector.k_effective(Tkv)
-        with _Stage(self, "k:indexer", "gsa_b200/indexer"):
-            scores = ops.indexer_scores(parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias,
-                                        self.indexer.scale, q_pos0=q_pos0, tkv=Tkv,
-                                        fill_upper=False)
-        if q_rows.dtype == torch.bfloat16 and self.d_head == 128:
-            with _Stage(self, "k:topk", "gsa_b200/topk_select"):
-                _, _, bitmask = ops.topk_select(scores, k_eff, q_pos0=q_pos0, want_indices=False,
-                                                want_mask=False, want_bitmask=True)
+        bf16_tc = q_rows.dtype == torch.bfloat16 and self.d_head == 128
+        with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
+            idx, mask, bitmask = ops.indexer_topk(
+                parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
+                q_pos0=q_pos0, tkv=Tkv, want_indices=not bf16_tc, want_mask=not bf16_tc,
+                want_bitmask=bf16_tc)
+        if bf16_tc:
             with _Stage(self, "k:masked_attention", "gsa_b200/sparse_attn"):
                 out = ops.masked_attention(q_rows, k_all, v_all, bitmask, self.scale, H,
                                            og=parts["og"], q_pos0=q_pos0)
             return out
-        with _Stage(self, "k:topk", "gsa_b200/topk_select"):
-            idx, mask, _ = ops.topk_select(scores, k_eff, q_pos0=q_pos0, want_bitmask=False)
         d = self.d_head
         with _Stage(self, "k:gather_attention", "gsa_b200/sparse_attn"):
             attn = ops.gather_attention(q_rows.view(B, Tq, H, d), k_all.view(B, Tkv, H, d),

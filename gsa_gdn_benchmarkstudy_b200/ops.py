@@ -155,6 +155,44 @@ def fused_gated_indexer(q_idx, k_idx, w, bias, scale: float, causal: bool = True
     return s.contiguous() if s.stride(1) != Tkv else s
 
 
+def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+                 scale: float, k_sel: int, q_pos0: int = 0, tkv: int | None = None,
+                 want_indices: bool = False, want_mask: bool = False, want_bitmask: bool = True,
+                 workspace: torch.Tensor | None = None):
+    """Indexer + top-k in one C call; the scores live only in a scratch workspace.
+
+    Same inputs as ``indexer_scores``; outputs as ``topk_select``
+    (indices int32, mask bool, bitmask int32 words), unrequested ones None."""
+    _cuda(q_idx, k_idx, w, bias)
+    B, Tq, H_I, d_I = q_idx.shape
+    if q_idx.stride(3) != 1 or q_idx.stride(2) != d_I:
+        q_idx = q_idx.contiguous()
+    q3 = q_idx.as_strided((B, Tq, H_I * d_I), (q_idx.stride(0), q_idx.stride(1), 1))
+    Tkv = k_idx.shape[1] if tkv is None else tkv
+    code = _dtype_code(q_idx)
+    if k_idx.dtype != q_idx.dtype or w.dtype != q_idx.dtype:
+        raise ValueError("q_idx, k_idx and w must share a dtype")
+    qs, ks, ws = _rows(q3, H_I * d_I, "q_idx"), _rows(k_idx, d_I, "k_idx"), _rows(w, H_I, "w")
+    bias32 = bias.detach().to(torch.float32).contiguous()
+    lib = _lib.load()
+    need = int(lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q_idx.device)
+    dev = q_idx.device
+    idx = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.int32) if want_indices else None
+    msk = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.uint8) if want_mask else None
+    W = bitmask_words(Tkv)
+    bm = torch.empty(B, Tq, W, device=dev, dtype=torch.int32) if want_bitmask else None
+    rc = lib.gsa_indexer_topk(
+        q3.data_ptr(), qs, k_idx.data_ptr(), ks, w.data_ptr(), ws, bias32.data_ptr(), float(scale),
+        code, B, Tq, Tkv, int(q_pos0), H_I, d_I, int(k_sel), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(),
+        idx.data_ptr() if idx is not None else None, msk.data_ptr() if msk is not None else None,
+        bm.data_ptr() if bm is not None else None, W, _stream())
+    _lib.check(rc, "gsa_indexer_topk")
+    return idx, (msk.bool() if msk is not None else None), bm
+
+
 # --------------------------------------------------------------------------- top-k
 def topk_select(scores: torch.Tensor, k_sel: int, q_pos0: int = 0, want_indices: bool = True,
                 want_mask: bool = True, want_bitmask: bool = True):

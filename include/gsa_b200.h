@@ -140,6 +140,29 @@ GSA_API int gsa_topk_select(const float* scores, int64_t score_stride,
  * expect for a key range of Tkv. */
 GSA_API int64_t gsa_bitmask_words(int Tkv);
 
+/* Bytes of caller-owned scratch that gsa_indexer_topk needs (the causal
+ * score rows of the call: B * Tq rows of round-up-to-4(Tkv) floats). */
+GSA_API int64_t gsa_indexer_topk_workspace_size(int B, int Tq, int Tkv);
+
+/*
+ * Indexer scores followed by top-k selection in one call: the forward's
+ * GatedLightningIndexer.forward (gsa_ref.py:97-126) + AdaptiveTopKSelector
+ * (gsa_ref.py:138-150), the pair the reference runs back to back at
+ * gsa_ref.py:303-308 / gsa_opt.py:664-677.  The [B,Tq,Tkv] score rows exist
+ * only in `workspace` (workspace_bytes >= gsa_indexer_topk_workspace_size);
+ * only their causal part is written and read.  Arguments as for
+ * gsa_indexer_scores and gsa_topk_select (any of indices / mask / bitmask
+ * may be NULL).
+ */
+GSA_API int gsa_indexer_topk(const void* q, int64_t q_stride,
+                             const void* k, int64_t k_stride,
+                             const void* w, int64_t w_stride,
+                             const float* bias, float scale, int dtype,
+                             int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                             int k_sel, void* workspace, int64_t workspace_bytes,
+                             int32_t* indices, uint8_t* mask,
+                             uint32_t* bitmask, int64_t bitmask_words, void* stream);
+
 /*
  * Sparse attention over a selection bitmask, on tcgen05 tensor cores.
  * Replaces _gather_along_seq + sparse_attention_ref (gsa_ref.py:185-238),

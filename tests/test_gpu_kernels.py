@@ -292,3 +292,25 @@ def test_gather_attention_vs_oracle(dtype):
     assert torch.equal(got[0, 7], torch.zeros_like(got[0, 7]))
     atol = 2e-2 if dtype == torch.bfloat16 else 1e-5
     _check_close(got, ref, atol=atol)
+
+
+# ──────────────────────────────────────────────────────────── fused indexer + top-k
+@pytest.mark.parametrize("B,Tq,Tkv,q_pos0,k_sel", [(2, 160, 160, 0, 48), (1, 700, 1500, 800, 256),
+                                                   (1, 2048, 2048, 0, 2048)])
+def test_indexer_topk_matches_separate_calls(B, Tq, Tkv, q_pos0, k_sel):
+    q, k, w, bias = _indexer_inputs(B, Tq, Tkv, torch.bfloat16, seed=Tq)
+    qc, kc, wc, bc = q.cuda(), k.cuda(), w.cuda(), bias.cuda()
+    scores = ops.indexer_scores(qc, kc, wc, bc, 0.125, q_pos0=q_pos0, tkv=Tkv, fill_upper=False)
+    i1, m1, b1 = ops.topk_select(scores, k_sel, q_pos0=q_pos0)
+    i2, m2, b2 = ops.indexer_topk(qc, kc, wc, bc, 0.125, k_sel, q_pos0=q_pos0, tkv=Tkv,
+                                  want_indices=True, want_mask=True, want_bitmask=True)
+    assert torch.equal(i1, i2) and torch.equal(m1, m2) and torch.equal(b1, b2)
+
+
+def test_indexer_topk_rejects_small_workspace():
+    lib = _lib.load()
+    need = lib.gsa_indexer_topk_workspace_size(1, 100, 100)
+    assert need == 100 * 100 * 4
+    rc = lib.gsa_indexer_topk(None, 256, None, 64, None, 4, None, 0.125, 0, 1, 100, 100, 0, 4, 64,
+                              16, 4096, need - 4, None, None, None, 4, None)
+    assert rc == 1
