@@ -42,6 +42,11 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _f32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
          _i32, _vp, _i64, _vp, _vp, _vp, _i64, _vp],
     ),
+    "gsa_indexer_topk_noalloc": (
+        _i32,
+        [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _f32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+         _i32, _vp, _vp, _vp, _i64, _vp],
+    ),
     "gsa_topk_select": (
         _i32,
         [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _vp],

@@ -16,6 +16,13 @@ thread_local char g_last_error[256] = "";
 // Device word that kernels set when a bounded wait expires.
 __device__ int g_dev_err;
 
+// Built-in scratch of gsa_indexer_topk_noalloc: the score rows that
+// gsa_indexer_topk otherwise keeps in the caller's workspace.  Every GPU that
+// loads the library holds it until the process exits.  In host code this name
+// stands for the host-side shadow, not a device address: kernels receive the
+// address that noalloc_scratch() looks up per device.
+static __device__ __align__(256) float g_noalloc_scratch[GSA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
 int set_cuda_error(cudaError_t e) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e),
                 cudaGetErrorString(e));
@@ -60,6 +67,30 @@ int device_state(DeviceState** out) {
   }
   if (!st.sm100) return set_error(GSA_ERR_NO_DEVICE, "current device is not sm_100 (B200)");
   *out = &st;
+  return GSA_OK;
+}
+
+// Device address of g_noalloc_scratch on the current device.  Looked up once
+// per device (with that device current) on the first gsa_indexer_topk_noalloc
+// call there; the lookup allocates nothing.
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  if (dev < 0 || dev >= kMaxDevices) return set_error(GSA_ERR_NO_DEVICE, "device index out of range");
+  if (!g_noalloc_ptr[dev]) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      float* p = nullptr;
+      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch);
+      if (e != cudaSuccess) return set_cuda_error(e);
+      g_noalloc_ptr[dev] = p;
+    }
+  }
+  *out = g_noalloc_ptr[dev];
   return GSA_OK;
 }
 
@@ -278,6 +309,32 @@ int gsa_indexer_topk(const void* q, int64_t q_stride, const void* k, int64_t k_s
   return indexer_topk_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
                            q_pos0, H_I, d_I, k_sel, static_cast<float*>(workspace), indices, mask,
                            bitmask, bitmask_words, static_cast<cudaStream_t>(stream));
+}
+
+int gsa_indexer_topk_noalloc(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                             const void* w, int64_t w_stride, const float* bias, float scale,
+                             int dtype, int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                             int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                             int64_t bitmask_words, void* stream) {
+  if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0 || k_sel <= 0 || k_sel > Tkv)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes (need 0 < k_sel <= Tkv)");
+  if (B == 0 || Tq == 0) return GSA_OK;
+  const int64_t need = gsa_indexer_topk_workspace_size(B, Tq, Tkv);
+  if (need > static_cast<int64_t>(GSA_NOALLOC_SCRATCH_BYTES)) {
+    std::snprintf(g_last_error, sizeof(g_last_error),
+                  "gsa_indexer_topk_noalloc needs %lld bytes of scratch, more than its built-in "
+                  "%lld; call gsa_indexer_topk with a workspace instead",
+                  static_cast<long long>(need), static_cast<long long>(GSA_NOALLOC_SCRATCH_BYTES));
+    return GSA_ERR_UNSUPPORTED;
+  }
+  if (bitmask && bitmask_words < gsa_bitmask_words(Tkv))
+    return set_error(GSA_ERR_INVALID_ARG, "bitmask_words < gsa_bitmask_words(Tkv)");
+  float* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return indexer_topk_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
+                           q_pos0, H_I, d_I, k_sel, scratch, indices, mask, bitmask,
+                           bitmask_words, static_cast<cudaStream_t>(stream));
 }
 
 int gsa_topk_select(const float* scores, int64_t score_stride, int B, int Tq, int Tkv, int q_pos0,

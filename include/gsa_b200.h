@@ -163,6 +163,46 @@ GSA_API int gsa_indexer_topk(const void* q, int64_t q_stride,
                              int32_t* indices, uint8_t* mask,
                              uint32_t* bitmask, int64_t bitmask_words, void* stream);
 
+/* Size of the library's built-in scratch buffer for gsa_indexer_topk_noalloc. */
+#define GSA_NOALLOC_SCRATCH_BYTES (16ll << 20)
+
+/*
+ * gsa_indexer_topk for callers that cannot allocate device memory.
+ * This entry point has no counterpart in the reference.
+ *
+ * Some callers may not call cudaMalloc. Examples: a plugin inside a host
+ * engine that owns every byte of device memory, or a runtime that fixes its
+ * memory budget at start-up, since an allocation can synchronise the device
+ * and fragment the pool. Such callers cannot provide the scratch that
+ * gsa_indexer_topk takes as `workspace`. This variant keeps that scratch
+ * instead in a buffer compiled into the library: GSA_NOALLOC_SCRATCH_BYTES
+ * (16 MiB) on every GPU that loads the library, held until the process exits.
+ * The caller still passes all inputs and outputs. Arguments are those of
+ * gsa_indexer_topk without workspace / workspace_bytes.
+ *
+ *   - Size limit: the call needs gsa_indexer_topk_workspace_size(B, Tq, Tkv)
+ *     bytes (B * Tq rows of round-up-to-4(Tkv) floats; e.g. one 2048-token
+ *     sequence).  Larger calls return GSA_ERR_UNSUPPORTED and say so in
+ *     gsa_last_error_string(); use gsa_indexer_topk with a workspace then.
+ *   - First call on a device: it looks up the device address of the buffer,
+ *     once per device, with that device current.  Make that first call before
+ *     any stream capture.
+ *   - Shared state: every call on a device uses the same buffer, which keeps
+ *     the scores of the last call.  Nothing in it needs to start at zero,
+ *     because each call writes every score it reads.  Calls whose work
+ *     overlaps on the GPU (e.g. on two streams) race on the buffer; order
+ *     them on one stream or use gsa_indexer_topk.
+ *   - Allocation: no cudaMalloc, cudaFree or allocating library routine is
+ *     called.
+ */
+GSA_API int gsa_indexer_topk_noalloc(const void* q, int64_t q_stride,
+                                     const void* k, int64_t k_stride,
+                                     const void* w, int64_t w_stride,
+                                     const float* bias, float scale, int dtype,
+                                     int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                                     int k_sel, int32_t* indices, uint8_t* mask,
+                                     uint32_t* bitmask, int64_t bitmask_words, void* stream);
+
 /*
  * Sparse attention over a selection bitmask, on tcgen05 tensor cores.
  * Replaces _gather_along_seq + sparse_attention_ref (gsa_ref.py:185-238),
