@@ -5,9 +5,13 @@
 //
 // Reference: GatedLightningIndexer.forward, gsa_ref.py:97-126 (fp32 math on
 // bf16-rounded projections; einsum, *scale, +bias, sigmoid, *sigmoid(w),
-// sum over heads in order h = 0..3, masked_fill(-inf)).  The op order of the
-// epilogue below follows those lines: z = fl(fl(dot*scale) + bias),
-// acc = fl(acc + fl(sigmoid(z) * sigmoid(w))).
+// sum over heads in order h = 0..3, masked_fill(-inf)).  The tensor-core
+// epilogue evaluates the same terms two keys at a time with f32x2 FMAs:
+// y = dot*(-scale*log2 e) + (-bias*log2 e), sigmoid = 1/(1 + 2^y) with 2^y on
+// the MUFU and the reciprocal by Newton-Raphson on the FMA pipe (common.cuh,
+// sigmoid2_nr), acc += sigmoid * sigmoid(w) in head order; about 1e-7 from the
+// reference's separately rounded fp32 ops.  The fp32 CUDA-core kernel keeps
+// the reference's exact op order.
 //
 // bf16 path: tcgen05 tensor cores.  One CTA owns 128 query rows and a chunk
 // of up to 512 keys.  Q (4 heads x [128 x 64] bf16) is loaded once by TMA
@@ -36,6 +40,7 @@ constexpr int kIdxQBytes = kIdxBM * kIdxD * 2;    // 16 KB per head
 constexpr int kIdxKBytes = kIdxBN * kIdxD * 2;    // 4 KB per stage
 constexpr int kIdxTmemCols = 256;                 // 2 buffers x 4 heads x 32
 constexpr int kIdxThreads = 192;                  // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr float kLog2e = 1.4426950408889634f;
 
 struct IdxSmem {
   uint64_t q_full;
@@ -164,18 +169,30 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
       const int buf = s & 1;
       if (!mbar_wait_warp(&sh->acc_full[buf], (s >> 1) & 1, a.err, abort)) break;
       tc_fence_after();
-      float acc[kIdxBN];
+      // score = sum_h sigmoid(w_h) * sigmoid(dot*scale + b_h), two keys per op:
+      // y = -(dot*scale + b_h)*log2(e), sigmoid = 1/(1 + 2^y)
+      uint64_t acc2[kIdxBN / 2];
 #pragma unroll
       for (int h = 0; h < kIdxHeads; ++h) {
         uint32_t raw[32];
         tmem_ld32(tmem + lane_base + buf * 128 + h * kIdxBN, raw);
         tc_wait_ld();
+        const uint64_t ys = f2_pack(-a.scale * kLog2e, -a.scale * kLog2e);
+        const uint64_t yb = f2_pack(-bh[h] * kLog2e, -bh[h] * kLog2e);
+        const uint64_t w2 = f2_pack(sw[h], sw[h]);
 #pragma unroll
-        for (int e = 0; e < kIdxBN; ++e) {
-          const float z = __fadd_rn(__fmul_rn(__uint_as_float(raw[e]), a.scale), bh[h]);
-          const float g = __fmul_rn(sigmoid_fast(z), sw[h]);
-          acc[e] = h == 0 ? g : __fadd_rn(acc[e], g);
+        for (int e = 0; e < kIdxBN; e += 2) {
+          const uint64_t y2 =
+              f2_fma(f2_pack(__uint_as_float(raw[e]), __uint_as_float(raw[e + 1])), ys, yb);
+          const uint64_t g2 = sigmoid2_nr(y2);
+          acc2[e >> 1] = h == 0 ? f2_fma(g2, w2, 0ull) : f2_fma(g2, w2, acc2[e >> 1]);
         }
+      }
+      float acc[kIdxBN];
+#pragma unroll
+      for (int e = 0; e < kIdxBN; e += 2) {
+        acc[e] = f2_lo(acc2[e >> 1]);
+        acc[e + 1] = f2_hi(acc2[e >> 1]);
       }
       tc_fence_before();
       __syncwarp();
