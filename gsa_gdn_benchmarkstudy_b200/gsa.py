@@ -236,6 +236,7 @@ class GatedSparseAttention(nn.Module):
         self._fused_weight: Optional[torch.Tensor] = None
         self._fused_bias: Optional[torch.Tensor] = None
         self._stage_events: Optional[list] = None
+        self._streams: dict = {}
         D, hi, di = hidden_size, n_idx_heads, d_indexer
         # Column layout of the fused projection output (gsa_opt.py:562-571 order).
         self._proj_sizes = [D, D, D, D, D, hi * di, di, hi]
@@ -298,6 +299,39 @@ class GatedSparseAttention(nn.Module):
             "ik": proj[..., o[6]:o[6] + di], "iw": proj[..., o[7]:o[7] + hi],
         }
 
+    def select_rows(self, parts: dict, ik_all: torch.Tensor, q_pos0: int,
+                    tkv: Optional[int] = None):
+        """Indexer + top-k for a block of query rows (``parts`` = the block's projection views).
+
+        Returns the selection: a bitmask [B, Tq, W] for the tensor-core attention
+        (bf16, d_head = 128), else (indices, mask) for the index-gather path."""
+        Tkv = ik_all.shape[1] if tkv is None else tkv
+        k_eff = self.topk_selector.k_effective(Tkv)
+        bf16_tc = parts["iq"].dtype == torch.bfloat16 and self.d_head == 128
+        with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
+            idx, mask, bitmask = ops.indexer_topk(
+                parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
+                q_pos0=q_pos0, tkv=Tkv, want_indices=not bf16_tc, want_mask=not bf16_tc,
+                want_bitmask=bf16_tc)
+        return bitmask if bf16_tc else (idx, mask)
+
+    def attend_selected(self, parts: dict, selection, k_all: torch.Tensor, v_all: torch.Tensor,
+                        q_rows: torch.Tensor, q_pos0: int) -> torch.Tensor:
+        """Sparse attention (+ output gate) of a block of query rows over its selection."""
+        B, Tq, D = q_rows.shape
+        Tkv = k_all.shape[1]
+        H, d = self.num_heads, self.d_head
+        if torch.is_tensor(selection):
+            with _Stage(self, "k:masked_attention", "gsa_b200/sparse_attn"):
+                return ops.masked_attention(q_rows, k_all, v_all, selection, self.scale, H,
+                                            og=parts["og"], q_pos0=q_pos0)
+        idx, mask = selection
+        with _Stage(self, "k:gather_attention", "gsa_b200/sparse_attn"):
+            attn = ops.gather_attention(q_rows.view(B, Tq, H, d), k_all.view(B, Tkv, H, d),
+                                        v_all.view(B, Tkv, H, d), idx, mask, self.scale)
+        with _Stage(self, "k:output_gate", "gsa_b200/output_gate"):
+            return ops.output_gate(attn.view(B, Tq, D), parts["og"])
+
     def attend_rows(self, parts: dict, k_all: torch.Tensor, v_all: torch.Tensor,
                     ik_all: torch.Tensor, q_rows: torch.Tensor, q_pos0: int) -> torch.Tensor:
         """Indexer -> top-k -> sparse attention (+ output gate) for a block of query rows.
@@ -306,28 +340,15 @@ class GatedSparseAttention(nn.Module):
         ``q_rows`` its RoPE'd queries [B, Tq, D]; ``k_all``/``v_all``/``ik_all``
         cover keys [0, Tkv).  Row r of the block is sequence position q_pos0 + r.
         Returns the gated attention output [B, Tq, D] (before o_proj)."""
-        B, Tq, D = q_rows.shape
-        Tkv = k_all.shape[1]
-        H = self.num_heads
-        k_eff = self.topk_selector.k_effective(Tkv)
-        bf16_tc = q_rows.dtype == torch.bfloat16 and self.d_head == 128
-        with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
-            idx, mask, bitmask = ops.indexer_topk(
-                parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
-                q_pos0=q_pos0, tkv=Tkv, want_indices=not bf16_tc, want_mask=not bf16_tc,
-                want_bitmask=bf16_tc)
-        if bf16_tc:
-            with _Stage(self, "k:masked_attention", "gsa_b200/sparse_attn"):
-                out = ops.masked_attention(q_rows, k_all, v_all, bitmask, self.scale, H,
-                                           og=parts["og"], q_pos0=q_pos0)
-            return out
-        d = self.d_head
-        with _Stage(self, "k:gather_attention", "gsa_b200/sparse_attn"):
-            attn = ops.gather_attention(q_rows.view(B, Tq, H, d), k_all.view(B, Tkv, H, d),
-                                        v_all.view(B, Tkv, H, d), idx, mask, self.scale)
-        with _Stage(self, "k:output_gate", "gsa_b200/output_gate"):
-            out = ops.output_gate(attn.view(B, Tq, D), parts["og"])
-        return out
+        sel = self.select_rows(parts, ik_all, q_pos0, tkv=k_all.shape[1])
+        return self.attend_selected(parts, sel, k_all, v_all, q_rows, q_pos0)
+
+    def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        s = self._streams.get(device)
+        if s is None:
+            s = torch.cuda.Stream(device=device)
+            self._streams[device] = s
+        return s
 
     def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
                 ) -> torch.Tensor:
@@ -342,10 +363,21 @@ class GatedSparseAttention(nn.Module):
             proj = self.project(x)
         parts = self.split(proj)
         cos, sin = self.rotary_emb(T, x.device, x.dtype)
+        # Two streams, as the reference's pipeline (gsa_opt.py:654-711): the
+        # indexer + top-k (tensor/MUFU-bound) run beside RoPE + value gate
+        # (HBM-bound); the attention waits for both.
+        main = torch.cuda.current_stream(x.device)
+        side = self._side_stream(x.device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            sel = self.select_rows(parts, parts["ik"], q_pos0=0)
         with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
             q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, self.num_heads,
                                      v_src=parts["v"], vg_src=parts["vg"])
-        attn = self.attend_rows(parts, k, v, parts["ik"], q, q_pos0=0)
+        main.wait_stream(side)
+        for t in (sel if isinstance(sel, tuple) else (sel,)):
+            t.record_stream(main)
+        attn = self.attend_selected(parts, sel, k, v, q, q_pos0=0)
         with _Stage(self, "lib:o_proj", "gsa_b200/o_proj"):
             out = F.linear(attn.view(B, T, D), self.o_proj.weight)
         _nvtx_pop()
