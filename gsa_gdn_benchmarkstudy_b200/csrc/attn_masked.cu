@@ -13,28 +13,34 @@
 // selection enters only as 16 bytes of bitmask per row per tile), instead
 // of gathering 2*k*H*d bytes per query row as the reference does.
 //
-// CTA = (batch b, head h, 128-query tile).  Warp roles:
+// CTA = (batch b, head h, 128-query tile), 12 warps in three warpgroups:
 //   warps 0-7  softmax + epilogue.  Warp w serves query rows 32(w%4)..+31
 //              (TMEM lane quarter w%4) over the key tiles of parity w/4:
 //              even tiles go to warps 0-3, odd tiles to warps 4-7, so each SM
 //              sub-partition runs two softmax warps on different tiles with no
 //              per-tile synchronisation between them.  Each parity keeps its own
 //              running max m, row sum l and TMEM accumulator O_par; the two are
-//              merged once in the epilogue.
-//   warp 8     TMA producer (Q once; K and V 128x128 tiles, 2-stage rings)
+//              merged once in the epilogue.  These warps raise their register
+//              budget to kSoftmaxRegs (setmaxnreg) so a whole 128-key row of S
+//              stays in registers.
+//   warp 8     TMA producer for Q and the K ring (2 stages)
 //   warp 9     TMEM owner + single-thread tcgen05.mma issuer
+//   warp 10    TMA producer for the V ring (2 stages), so K loads never queue
+//              behind V loads
+//   warp 11    idle (completes the third warpgroup for setmaxnreg)
 // Per key tile j (parity par = j % 2):
-//   MMA:      S_j = Q.K_j^T into TMEM S buffer par (issued one tile ahead);
+//   softmax:  load the row of S_j from TMEM into registers and release the S
+//             buffer at once (the MMA warp then computes S_{j+2} into it while
+//             this tile's exponentials run).  Unselected keys are set to -inf,
+//             the tile max t of the selected keys is taken, and the running
+//             max is raised lazily: m moves to max(m, t) only when that exceeds
+//             m by more than 8/c (c = scale*log2 e), so p = 2^(s*c - m*c) <= 2^8;
+//             when it moves, l and this warp's rows of O_par are scaled by
+//             2^((m_old - m_new)*c).  P (bf16) goes to shared buffer par in the
+//             128B-swizzled K-major layout the MMA reads, once P.V of tile j-2
+//             (same buffer, same O_par) has finished.
+//   MMA:      S_{j+2} = Q.K_{j+2}^T as soon as S_j is released, then
 //             O_par += P_j.V_j once P_j is in shared memory.
-//   softmax:  p = 2^(s*c - m*c), c = scale*log2(e), for selected keys, using the
-//             running max m of this parity without waiting for the tile max.
-//             m is raised only when some selected s*c - m*c exceeds 8 (p > 256):
-//             then the warp recomputes the tile's p from S with the new m and
-//             scales l and its rows of O_par by 2^((m_old - m_new)*c); the P.V of
-//             the previous tile of the same parity has finished by then.  A
-//             row's first selected keys set m from an exact tile max.
-//             P (bf16) goes to shared buffer par in the 128B-swizzled K-major
-//             layout the MMA reads.
 // Epilogue: M = max(m_even, m_odd), O = O_even*2^((m_even-M)c) + O_odd*2^((m_odd-M)c)
 //   (likewise l), o = O / l rounded to bf16; optional gate bf16(o * bf16(sigmoid(og))).
 //
@@ -50,16 +56,25 @@ constexpr int kAtBN = 128;
 constexpr int kAtD = 128;
 constexpr int kAtTileBytes = kAtBM * kAtD * 2;  // 32 KB: two 128x64 swizzled boxes
 constexpr int kAtBoxBytes = kAtTileBytes / 2;   // 16 KB
-constexpr int kAtThreads = 320;
+constexpr int kAtThreads = 384;
 constexpr int kAtTmemCols = 512;
-constexpr float kRescaleP = 256.0f;             // p may reach 2^8 before m is raised
+constexpr float kRescaleLog2 = 8.0f;            // p may reach 2^8 before m is raised
+// Register split (setmaxnreg): the launch gives 384 threads x 168 registers;
+// the control warpgroup drops to kCtrlRegs and the two softmax warpgroups take
+// the rest: 128*56 + 256*224 == 384*168.
+constexpr int kLaunchRegs = 168;
+constexpr int kCtrlRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(128 * kCtrlRegs + 256 * kSoftmaxRegs <= kAtThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
 
 struct AtSmem {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full[2], p_empty[2];
+  uint64_t k_full[2], v_full[2];
+  uint64_t s_full[2];   // S_j computed (also: K stage free)
+  uint64_t s_empty[2];  // S_j loaded into registers by the 4 softmax warps
+  uint64_t p_full[2];   // P_j written by the 4 softmax warps
+  uint64_t p_empty[2];  // P_j.V_j finished (also: V stage and P buffer free)
   uint64_t o_full;
   uint32_t tmem_base;
   int abort;
@@ -78,96 +93,19 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-// Masked max of this thread's row of one S tile (raw dot-product units).
-__device__ __forceinline__ float row_tile_max(uint32_t s_taddr, const uint32_t (&wb)[4]) {
-  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-  for (int cc = 0; cc < 4; ++cc) {
-    uint32_t sv[32];
-    tmem_ld32(s_taddr + cc * 32, sv);
-    tc_wait_ld();
-#pragma unroll
-    for (int e = 0; e < 32; ++e)
-      if ((wb[cc] >> e) & 1u) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sv[e]));
-  }
-  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
-// One pass over this thread's row of an S tile: p = 2^(s*c - m*c) for the
-// selected keys (0 elsewhere) goes, as bf16, into row i of the swizzled P
-// tile at pb.  Returns the row sum of p; `over` is set when some p exceeds
-// kRescaleP (the running max m must then be raised).
-__device__ __forceinline__ float row_exp_pass(uint32_t s_taddr, const uint32_t (&wb)[4], float c,
-                                              float m, uint32_t pb, int i, bool& over) {
-  const float mc = (m == -INFINITY) ? 0.f : m * c;
-  const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
-  uint64_t l2a = 0, l2b = 0;  // packed partial row sums
-  uint32_t pmax = 0;          // packed bf16 max of p (p >= 0)
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {
-    uint32_t sv[32];
-    tmem_ld32(s_taddr + cc * 32, sv);
-    tc_wait_ld();
-    uint32_t packed[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 2) {
-      const uint64_t x2 =
-          f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2, nmc2);
-      const float p0 = ((wb[cc] >> e) & 1u) ? fast_ex2(f2_lo(x2)) : 0.f;
-      const float p1 = ((wb[cc] >> (e + 1)) & 1u) ? fast_ex2(f2_hi(x2)) : 0.f;
-      if (e & 2) l2b = f2_add(l2b, f2_pack(p0, p1));
-      else l2a = f2_add(l2a, f2_pack(p0, p1));
-      packed[e >> 1] = pack_bf16x2(p0, p1);
-      pmax = bf2_max(pmax, packed[e >> 1]);
-    }
-    // keys 32cc..32cc+31 -> box cc/2, 16-byte chunks 4*(cc%2) .. +3 of row i
-    const uint32_t box = pb + (cc >> 1) * kAtBoxBytes;
-#pragma unroll
-    for (int qd = 0; qd < 4; ++qd)
-      st_shared_v4(box + sw128_offset(i, (cc & 1) * 4 + qd), packed[4 * qd], packed[4 * qd + 1],
-                   packed[4 * qd + 2], packed[4 * qd + 3]);
-  }
-  const float pm = fmaxf(__uint_as_float(pmax << 16), __uint_as_float(pmax & 0xFFFF0000u));
-  over = pm > kRescaleP;
-  const uint64_t l2 = f2_add(l2a, l2b);
-  return f2_lo(l2) + f2_hi(l2);
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
-
-struct RowState {
-  float m, l, lt;
-};
-
-// Rare path, kept out of line so the hot loop is not duplicated: rows whose p
-// overshot raise m to the exact tile max; l and this warp's O rows (earlier
-// tiles of the same parity) are scaled by 2^((m_old - m_new) c); then the
-// tile's p are recomputed.  All lanes of the warp call it together.
-__device__ __noinline__ RowState row_rescale_redo(uint32_t s_taddr, uint32_t o_taddr, uint32_t w0,
-                                                  uint32_t w1, uint32_t w2, uint32_t w3, float c,
-                                                  float m, float l, bool over, int j,
-                                                  uint32_t pb, int i) {
-  const uint32_t wb[4] = {w0, w1, w2, w3};
-  const float tm = row_tile_max(s_taddr, wb);
-  float alpha = 1.f;
-  if (over) {
-    alpha = fast_ex2((m - tm) * c);
-    m = tm;
-  }
-  l *= alpha;
-  if (j >= 2) {  // O of this parity holds P.V of earlier tiles
-#pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t ov[32];
-      tmem_ld32(o_taddr + cc * 32, ov);
-      tc_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-      tmem_st32(o_taddr + cc * 32, ov);
-    }
-    tc_wait_st();
-  }
-  bool over2;
-  const float lt = row_exp_pass(s_taddr, wb, c, m, pb, i, over2);
-  return RowState{m, l, lt};
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __global__ void __launch_bounds__(kAtThreads, 1)
@@ -201,9 +139,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     mbar_init(&sh->q_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sh->k_full[s], 1);
-      mbar_init(&sh->k_empty[s], 1);
       mbar_init(&sh->v_full[s], 1);
-      mbar_init(&sh->v_empty[s], 1);
       mbar_init(&sh->s_full[s], 1);
       mbar_init(&sh->s_empty[s], 4);
       mbar_init(&sh->p_full[s], 4);
@@ -223,83 +159,100 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const uint32_t tmem = sh->tmem_base;
   volatile int* abort = &sh->abort;
 
-  if (warp == 8) {
-    // ---------------------------------------------------------- TMA producer
-    if (lane == 0) {
+  if (warp >= 8) {
+    reg_dealloc<kCtrlRegs>();
+    const int x0 = h * kAtD;
+    if (warp == 8 && lane == 0) {
+      // ------------------------------------------------ TMA: Q once, K ring
       prefetch_tmap(&qmap);
       prefetch_tmap(&kmap);
-      prefetch_tmap(&vmap);
-      const int x0 = h * kAtD;
       mbar_arrive_expect_tx(&sh->q_full, kAtTileBytes);
       tma_load_3d(q_s, &qmap, x0, row0, b, &sh->q_full);
       tma_load_3d(q_s + kAtBoxBytes, &qmap, x0 + 64, row0, b, &sh->q_full);
       for (int j = 0; j < nt; ++j) {
         const int st = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait(&sh->k_empty[st], ph, a.err, abort)) break;
+        // stage st is free once S_{j-2} has been computed
+        if (!mbar_wait(&sh->s_full[st], ((j >> 1) & 1) ^ 1, a.err, abort)) break;
         uint8_t* kd = k_s + st * kAtTileBytes;
         mbar_arrive_expect_tx(&sh->k_full[st], kAtTileBytes);
         tma_load_3d(kd, &kmap, x0, j * kAtBN, b, &sh->k_full[st]);
         tma_load_3d(kd + kAtBoxBytes, &kmap, x0 + 64, j * kAtBN, b, &sh->k_full[st]);
-        if (!mbar_wait(&sh->v_empty[st], ph, a.err, abort)) break;
+      }
+    } else if (warp == 10 && lane == 0) {
+      // ------------------------------------------------ TMA: V ring
+      prefetch_tmap(&vmap);
+      for (int j = 0; j < nt; ++j) {
+        const int st = j & 1;
+        // stage st is free once P_{j-2}.V_{j-2} has finished
+        if (!mbar_wait(&sh->p_empty[st], ((j >> 1) & 1) ^ 1, a.err, abort)) break;
         uint8_t* vd = v_s + st * kAtTileBytes;
         mbar_arrive_expect_tx(&sh->v_full[st], kAtTileBytes);
         tma_load_3d(vd, &vmap, x0, j * kAtBN, b, &sh->v_full[st]);
         tma_load_3d(vd + kAtBoxBytes, &vmap, x0 + 64, j * kAtBN, b, &sh->v_full[st]);
       }
-    }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(kAtBM, kAtBN, 0, 0);  // Q, K both K-major
-      constexpr uint32_t idesc_o = idesc_bf16_f32(kAtBM, kAtD, 0, 1);   // P K-major, V MN-major
-      const uint32_t q_base = smem_u32(q_s);
-      const uint32_t k_base = smem_u32(k_s);
-      const uint32_t v_base = smem_u32(v_s);
-      const uint32_t p_base = smem_u32(p_s);
-      bool ok = mbar_wait(&sh->q_full, 0, a.err, abort);
+    } else if (warp == 9) {
+      // ------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_bf16_f32(kAtBM, kAtBN, 0, 0);  // Q, K both K-major
+        constexpr uint32_t idesc_o = idesc_bf16_f32(kAtBM, kAtD, 0, 1);   // P K-major, V MN-major
+        const uint32_t q_base = smem_u32(q_s);
+        const uint32_t k_base = smem_u32(k_s);
+        const uint32_t v_base = smem_u32(v_s);
+        const uint32_t p_base = smem_u32(p_s);
+        bool ok = mbar_wait(&sh->q_full, 0, a.err, abort);
 
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&sh->k_full[st], ph, a.err, abort)) return false;
-        if (!mbar_wait(&sh->s_empty[st], ph ^ 1, a.err, abort)) return false;
-        tc_fence_after();
+        // S_j = Q.K_j^T into S buffer j%2 (free: S_{j-2} was loaded by the softmax)
+        auto issue_s = [&](int j) -> bool {
+          const int st = j & 1;
+          if (!mbar_wait(&sh->k_full[st], (j >> 1) & 1, a.err, abort)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kAtD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kAtBoxBytes + (kk & 3) * 32;
-          const uint64_t ad = sdesc_sw128(q_base + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(k_base + st * kAtTileBytes + off, 16, 1024);
-          tc_mma_ss(tmem + st * kAtBN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(&sh->s_full[st]);
-        tc_commit(&sh->k_empty[st]);
-        return true;
-      };
+          for (int kk = 0; kk < kAtD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kAtBoxBytes + (kk & 3) * 32;
+            const uint64_t ad = sdesc_sw128(q_base + off, 16, 1024);
+            const uint64_t bd = sdesc_sw128(k_base + st * kAtTileBytes + off, 16, 1024);
+            tc_mma_ss(tmem + st * kAtBN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&sh->s_full[st]);
+          return true;
+        };
+        // O_par += P_j.V_j
+        auto issue_pv = [&](int j) -> bool {
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&sh->p_full[st], ph, a.err, abort)) return false;
+          if (!mbar_wait(&sh->v_full[st], ph, a.err, abort)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kAtBN / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(
+                p_base + st * kAtTileBytes + (kk >> 2) * kAtBoxBytes + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd =
+                sdesc_sw128(v_base + st * kAtTileBytes + kk * 16 * 128, kAtBoxBytes, 1024);
+            tc_mma_ss(tmem + (2 + st) * kAtBN, ad, bd, idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&sh->p_empty[st]);
+          return true;
+        };
 
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < nt; ++j) {
-        if (j + 1 < nt && !(ok = issue_s(j + 1))) break;
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&sh->v_full[st], ph, a.err, abort)) { ok = false; break; }
-        if (!mbar_wait(&sh->p_full[st], ph, a.err, abort)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kAtBN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(
-              p_base + st * kAtTileBytes + (kk >> 2) * kAtBoxBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd =
-              sdesc_sw128(v_base + st * kAtTileBytes + kk * 16 * 128, kAtBoxBytes, 1024);
-          tc_mma_ss(tmem + (2 + st) * kAtBN, ad, bd, idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
+        if (ok) ok = issue_s(0);
+        if (ok && nt > 1) ok = issue_s(1);
+        // Expected event order: S_j released, then P_{j-1} written (the two
+        // parities run half a tile apart), so S_{j+2} goes first.
+        for (int j = 0; ok && j < nt; ++j) {
+          if (j + 2 < nt) {
+            ok = mbar_wait(&sh->s_empty[j & 1], (j >> 1) & 1, a.err, abort) && issue_s(j + 2);
+            if (!ok) break;
+          }
+          if (j >= 1 && !(ok = issue_pv(j - 1))) break;
         }
-        tc_commit(&sh->p_empty[st]);
-        tc_commit(&sh->v_empty[st]);
+        if (ok) ok = issue_pv(nt - 1);
+        if (ok) tc_commit(&sh->o_full);
       }
-      if (ok) tc_commit(&sh->o_full);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
+    reg_alloc<kSoftmaxRegs>();
     // ---------------------------------------------------------- softmax warps
     const int quarter = warp & 3;
     const int par = warp >> 2;           // key-tile parity served by this warp
@@ -312,6 +265,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     const uint32_t s_taddr = tmem + lane_base + par * kAtBN;
     const uint32_t o_taddr = tmem + lane_base + (2 + par) * kAtBN;
     const float c = a.scale * 1.4426950408889634f;
+    const uint64_t c2 = f2_pack(c, c);
     const uint32_t pb = smem_u32(p_s) + par * kAtTileBytes;
     bool ok = true;
     float m = -INFINITY;   // running max of this parity (raw dot-product units)
@@ -325,30 +279,88 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       const uint32_t wb[4] = {bits.x, bits.y, bits.z, bits.w};
       if (!(ok = mbar_wait_warp(&sh->s_full[par], ph, a.err, abort))) break;
       tc_fence_after();
-      // a row's first selected keys: start m from the exact tile max
-      if (__any_sync(0xFFFFFFFFu, row_ok && m == -INFINITY)) {
-        const float tm = row_tile_max(s_taddr, wb);
-        if (m == -INFINITY) m = tm;
+      uint32_t sv[4][32];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) tmem_ld32(s_taddr + cc * 32, sv[cc]);
+      tc_wait_ld();
+      // S_j is in registers: hand the buffer back for S_{j+2}
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->s_empty[par]);
+
+      // unselected keys -> -inf; tile max of the selected ones
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float s0 = ((wb[cc] >> e) & 1u) ? __uint_as_float(sv[cc][e]) : -INFINITY;
+          const float s1 = ((wb[cc] >> (e + 1)) & 1u) ? __uint_as_float(sv[cc][e + 1]) : -INFINITY;
+          sv[cc][e] = __float_as_uint(s0);
+          sv[cc][e + 1] = __float_as_uint(s1);
+          mx[(e >> 1) & 3] = max3f(mx[(e >> 1) & 3], s0, s1);
+        }
       }
+      const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      // lazy running max: move only when the tile max exceeds m by more than 8/c
+      const float m_old = m;
+      const bool raise = tmax > m_old && (m_old == -INFINITY || (tmax - m_old) * c > kRescaleLog2);
+      float alpha = 1.f;
+      if (raise) {
+        alpha = (m_old == -INFINITY) ? 0.f : fast_ex2((m_old - tmax) * c);
+        m = tmax;
+      }
+      const float mc = (m == -INFINITY) ? 0.f : m * c;
+      const uint64_t nmc2 = f2_pack(-mc, -mc);
+
+      // p = 2^(s*c - m*c) (0 at unselected keys), row sum, bf16 pack
+      uint64_t l2a = 0, l2b = 0;
+      uint32_t packed[4][16];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const uint64_t x2 = f2_fma(
+              f2_pack(__uint_as_float(sv[cc][e]), __uint_as_float(sv[cc][e + 1])), c2, nmc2);
+          const float p0 = fast_ex2(f2_lo(x2));
+          const float p1 = fast_ex2(f2_hi(x2));
+          if (e & 2) l2b = f2_add(l2b, f2_pack(p0, p1));
+          else l2a = f2_add(l2a, f2_pack(p0, p1));
+          packed[cc][e >> 1] = pack_bf16x2(p0, p1);
+        }
+      }
+      const uint64_t l2 = f2_add(l2a, l2b);
+
       // P buffer par is free (and O_par stable) once P.V of tile j-2 finished
       if (!(ok = mbar_wait_warp(&sh->p_empty[par], ph ^ 1, a.err, abort))) break;
-      bool over;
-      float lt = row_exp_pass(s_taddr, wb, c, m, pb, i, over);
-      if (__any_sync(0xFFFFFFFFu, over)) {
-        const RowState rs =
-            row_rescale_redo(s_taddr, o_taddr, wb[0], wb[1], wb[2], wb[3], c, m, l, over, j, pb, i);
-        m = rs.m;
-        l = rs.l;
-        lt = rs.lt;
+      tc_fence_after();
+      // O rows of earlier tiles of this parity follow a raised max (rare)
+      if (j >= 2 && __any_sync(0xFFFFFFFFu, raise && m_old != -INFINITY)) {
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t ov[32];
+          tmem_ld32(o_taddr + cc * 32, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(o_taddr + cc * 32, ov);
+        }
+        tc_wait_st();
       }
-      l += lt;
+      l = l * alpha + (f2_lo(l2) + f2_hi(l2));
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        // keys 32cc..32cc+31 -> box cc/2, 16-byte chunks 4*(cc%2) .. +3 of row i
+        const uint32_t box = pb + (cc >> 1) * kAtBoxBytes;
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd)
+          st_shared_v4(box + sw128_offset(i, (cc & 1) * 4 + qd), packed[cc][4 * qd],
+                       packed[cc][4 * qd + 1], packed[cc][4 * qd + 2], packed[cc][4 * qd + 3]);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sh->s_empty[par]);  // S_j consumed
-        mbar_arrive(&sh->p_full[par]);   // P_j ready
-      }
+      if (lane == 0) mbar_arrive(&sh->p_full[par]);  // P_j ready
     }
 
     // epilogue: merge the two parities, O / l (+ output gate), bf16 store of

@@ -1,5 +1,6 @@
 // capi.cu — the extern "C" entry points of include/gsa_b200.h: argument
 // checks, TMA tensor-map construction, dispatch to the kernels, status codes.
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -362,6 +363,8 @@ int gsa_masked_attention(const void* q, int64_t q_stride, const void* k, int64_t
   if (B < 0 || Tq < 0 || Tkv < 0 || q_pos0 < 0 || H <= 0 || d <= 0)
     return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
   if (d != 128) return set_error(GSA_ERR_UNSUPPORTED, "masked attention needs d == 128");
+  if (!(scale > 0.f) || !std::isfinite(scale))  // the lazy running max assumes scale > 0
+    return set_error(GSA_ERR_INVALID_ARG, "masked attention needs a finite scale > 0");
   if (B == 0 || Tq == 0 || Tkv == 0) return GSA_OK;
   if (!q || !k || !v || !bitmask || !out) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
   const int64_t width = static_cast<int64_t>(H) * d;

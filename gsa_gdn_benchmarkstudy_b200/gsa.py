@@ -237,6 +237,7 @@ class GatedSparseAttention(nn.Module):
         self._fused_bias: Optional[torch.Tensor] = None
         self._stage_events: Optional[list] = None
         self._streams: dict = {}
+        self._workspaces: dict = {}  # (device, stream) -> indexer/top-k scratch
         D, hi, di = hidden_size, n_idx_heads, d_indexer
         # Column layout of the fused projection output (gsa_opt.py:562-571 order).
         self._proj_sizes = [D, D, D, D, D, hi * di, di, hi]
@@ -308,11 +309,13 @@ class GatedSparseAttention(nn.Module):
         Tkv = ik_all.shape[1] if tkv is None else tkv
         k_eff = self.topk_selector.k_effective(Tkv)
         bf16_tc = parts["iq"].dtype == torch.bfloat16 and self.d_head == 128
+        B, Tq = parts["iq"].shape[:2]
+        ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc)
         with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
             idx, mask, bitmask = ops.indexer_topk(
                 parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
                 q_pos0=q_pos0, tkv=Tkv, want_indices=not bf16_tc, want_mask=not bf16_tc,
-                want_bitmask=bf16_tc)
+                want_bitmask=bf16_tc, workspace=ws, bitmask_out=bm)
         return bitmask if bf16_tc else (idx, mask)
 
     def attend_selected(self, parts: dict, selection, k_all: torch.Tensor, v_all: torch.Tensor,
@@ -342,6 +345,28 @@ class GatedSparseAttention(nn.Module):
         Returns the gated attention output [B, Tq, D] (before o_proj)."""
         sel = self.select_rows(parts, ik_all, q_pos0, tkv=k_all.shape[1])
         return self.attend_selected(parts, sel, k_all, v_all, q_rows, q_pos0)
+
+    def _scratch(self, device: torch.device, B: int, Tq: int, Tkv: int, want_bitmask: bool):
+        """Score scratch and selection bitmask for indexer + top-k, kept per
+        (device, current stream).
+
+        Reusing them keeps a 1 GiB-scale allocation (T=16K) out of every
+        forward.  Work on one stream runs in order, so a later call cannot
+        overwrite scores an earlier call still reads.  The bitmask is read by
+        the attention of the same forward; a later selection on the side
+        stream waits for that attention (``side.wait_stream(main)`` at the top
+        of ``forward``), and ``attend_rows`` selects and attends on one stream."""
+        need = ops.indexer_topk_workspace_size(B, Tq, Tkv)
+        key = (device, torch.cuda.current_stream(device).cuda_stream)
+        ws, bm = self._workspaces.get(key, (None, None))
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(need, dtype=torch.uint8, device=device)
+        shape = (B, Tq, ops.bitmask_words(Tkv))
+        n_words = B * Tq * shape[2]
+        if want_bitmask and (bm is None or bm.numel() < n_words):
+            bm = torch.empty(n_words, dtype=torch.int32, device=device)
+        self._workspaces[key] = (ws, bm)
+        return ws, (bm[:n_words].view(shape) if want_bitmask else None)
 
     def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
         s = self._streams.get(device)
@@ -375,8 +400,9 @@ class GatedSparseAttention(nn.Module):
             q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, self.num_heads,
                                      v_src=parts["v"], vg_src=parts["vg"])
         main.wait_stream(side)
-        for t in (sel if isinstance(sel, tuple) else (sel,)):
-            t.record_stream(main)
+        if isinstance(sel, tuple):  # index lists are new tensors; the bitmask is kept scratch
+            for t in sel:
+                t.record_stream(main)
         attn = self.attend_selected(parts, sel, k, v, q, q_pos0=0)
         with _Stage(self, "lib:o_proj", "gsa_b200/o_proj"):
             out = F.linear(attn.view(B, T, D), self.o_proj.weight)

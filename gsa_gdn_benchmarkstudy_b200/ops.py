@@ -67,6 +67,11 @@ def bitmask_words(tkv: int) -> int:
     return int(_lib.load().gsa_bitmask_words(int(tkv)))
 
 
+def indexer_topk_workspace_size(B: int, Tq: int, Tkv: int) -> int:
+    """Bytes of scratch ``indexer_topk`` needs (the fp32 score rows)."""
+    return int(_lib.load().gsa_indexer_topk_workspace_size(int(B), int(Tq), int(Tkv)))
+
+
 # --------------------------------------------------------------------------- RoPE + G2
 def rope_gates(q_src: torch.Tensor, k_src: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                num_heads: int, v_src: torch.Tensor | None = None,
@@ -158,11 +163,13 @@ def fused_gated_indexer(q_idx, k_idx, w, bias, scale: float, causal: bool = True
 def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
                  scale: float, k_sel: int, q_pos0: int = 0, tkv: int | None = None,
                  want_indices: bool = False, want_mask: bool = False, want_bitmask: bool = True,
-                 workspace: torch.Tensor | None = None):
+                 workspace: torch.Tensor | None = None, bitmask_out: torch.Tensor | None = None):
     """Indexer + top-k in one C call; the scores live only in a scratch workspace.
 
     Same inputs as ``indexer_scores``; outputs as ``topk_select``
-    (indices int32, mask bool, bitmask int32 words), unrequested ones None."""
+    (indices int32, mask bool, bitmask int32 words), unrequested ones None.
+    ``bitmask_out`` (int32 [B, Tq, bitmask_words(Tkv)], contiguous) receives the
+    bitmask instead of a new tensor."""
     _cuda(q_idx, k_idx, w, bias)
     B, Tq, H_I, d_I = q_idx.shape
     if q_idx.stride(3) != 1 or q_idx.stride(2) != d_I:
@@ -182,7 +189,16 @@ def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias
     idx = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.int32) if want_indices else None
     msk = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.uint8) if want_mask else None
     W = bitmask_words(Tkv)
-    bm = torch.empty(B, Tq, W, device=dev, dtype=torch.int32) if want_bitmask else None
+    bm = None
+    if want_bitmask:
+        if bitmask_out is not None:
+            if (bitmask_out.shape != (B, Tq, W) or bitmask_out.dtype != torch.int32
+                    or not bitmask_out.is_contiguous() or bitmask_out.device != dev):
+                raise ValueError(f"bitmask_out must be a contiguous int32 [{B}, {Tq}, {W}] "
+                                 "tensor on the inputs' device")
+            bm = bitmask_out
+        else:
+            bm = torch.empty(B, Tq, W, device=dev, dtype=torch.int32)
     rc = lib.gsa_indexer_topk(
         q3.data_ptr(), qs, k_idx.data_ptr(), ks, w.data_ptr(), ws, bias32.data_ptr(), float(scale),
         code, B, Tq, Tkv, int(q_pos0), H_I, d_I, int(k_sel), workspace.data_ptr(),

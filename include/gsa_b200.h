@@ -218,7 +218,8 @@ GSA_API int gsa_indexer_topk_noalloc(const void* q, int64_t q_stride,
  *   bitmask [B, Tq, bitmask_words] uint32 as written by gsa_topk_select
  *   og  [B, Tq, H*d] output-gate logits (bias added), row stride og_stride, or NULL
  *   out [B, Tq, H*d] row stride out_stride (bf16)
- * Requires bf16, d == 128, 16-byte aligned rows.
+ * Requires bf16, d == 128, 16-byte aligned rows, and a finite scale > 0
+ * (GSA_ERR_INVALID_ARG otherwise).
  */
 GSA_API int gsa_masked_attention(const void* q, int64_t q_stride,
                          const void* k, int64_t k_stride,

@@ -259,6 +259,35 @@ def test_masked_attention_vs_oracle(B, T, H, k_sel):
     assert rel < 1e-2
 
 
+def test_masked_attention_raised_max_paths():
+    # Logits grow along the key axis, so each row's running max is raised
+    # several times after O already holds earlier tiles (O rows rescaled);
+    # no key before 300 is selectable, so rows past 300 take their first max
+    # late, and rows before 300 have no selected key at all (zeros).
+    B, T, H = 1, 1100, 2
+    q, k, v, s, ks = _attn_case(B, T, H, seed=21, k_sel=256)
+    pos = torch.arange(T, dtype=torch.float32)
+    k[..., 0] = (0.02 * pos).view(1, T, 1).to(k.dtype)
+    q[..., 0] = 8.0
+    s[:, :, :300] = NEG
+    idx, mask, bm = ops.topk_select(s.cuda(), ks)
+    scale = 128 ** -0.5
+    got = ops.masked_attention(q.cuda(), k.cuda(), v.cuda(), bm, scale, H).cpu()
+    ref = O.sparse_attention(q.float(), k.float(), v.float(), idx.cpu().long(), mask.cpu(), scale)
+    got = got.view(B, T, H, 128)
+    assert torch.equal(got[:, :300], torch.zeros_like(got[:, :300]))
+    _, rel = _check_close(got, ref, atol=2e-2)
+    assert rel < 1e-2
+
+
+def test_masked_attention_rejects_bad_scale():
+    q = torch.zeros(1, 8, 128, dtype=torch.bfloat16, device="cuda")
+    bm = torch.zeros(1, 8, 4, dtype=torch.int32, device="cuda")
+    for bad in (0.0, -0.1, float("inf"), float("nan")):
+        with pytest.raises(RuntimeError, match="scale"):
+            ops.masked_attention(q, q, q, bm, bad, 1)
+
+
 def test_masked_attention_row_block_and_gate():
     B, T, H = 1, 900, 2
     q, k, v, s, ks = _attn_case(B, T, H, seed=11, k_sel=100)
