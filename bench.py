@@ -362,7 +362,8 @@ def run_ours(args, cfg, rank: int, world: int, device):
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms, 4), "ms_per_step_median_rank0": round(e2e_median, 4)},
         "roofline": rl,
-        "stage_ms": {k[2:]: round(v, 4) for k, v in stage_avg.items()},
+        "stage_ms": {(k[2:] if k.startswith("k:") else k.split(":", 1)[1] + " (cuBLAS)"): round(v, 4)
+                     for k, v in stage_avg.items()},
         **extra,
     }
     if world == 1 and not args.no_cpu_baseline:

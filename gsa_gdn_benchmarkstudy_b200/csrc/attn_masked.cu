@@ -59,6 +59,7 @@ constexpr int kAtBoxBytes = kAtTileBytes / 2;   // 16 KB
 constexpr int kAtThreads = 384;
 constexpr int kAtTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;            // p may reach 2^8 before m is raised
+constexpr long long kDrainCycles = 200000000LL; // ~0.1 s: in-flight copies/MMAs after an abort
 // Register split (setmaxnreg): the launch gives 384 threads x 168 registers;
 // the control warpgroup drops to kCtrlRegs and the two softmax warpgroups take
 // the rest: 128*56 + 256*224 == 384*168.
@@ -76,6 +77,7 @@ struct AtSmem {
   uint64_t p_full[2];   // P_j written by the 4 softmax warps
   uint64_t p_empty[2];  // P_j.V_j finished (also: V stage and P buffer free)
   uint64_t o_full;
+  uint64_t drain;       // MMAs in flight when the CTA gives up
   uint32_t tmem_base;
   int abort;
   float xm[2][kAtBM];  // [parity][row] running max, for the epilogue merge
@@ -146,6 +148,7 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(&sh->p_empty[s], 1);
     }
     mbar_init(&sh->o_full, 1);
+    mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
@@ -169,7 +172,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_arrive_expect_tx(&sh->q_full, kAtTileBytes);
       tma_load_3d(q_s, &qmap, x0, row0, b, &sh->q_full);
       tma_load_3d(q_s + kAtBoxBytes, &qmap, x0 + 64, row0, b, &sh->q_full);
-      for (int j = 0; j < nt; ++j) {
+      int j = 0;
+      for (; j < nt; ++j) {
         const int st = j & 1;
         // stage st is free once S_{j-2} has been computed
         if (!mbar_wait(&sh->s_full[st], ((j >> 1) & 1) ^ 1, a.err, abort)) break;
@@ -178,10 +182,16 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         tma_load_3d(kd, &kmap, x0, j * kAtBN, b, &sh->k_full[st]);
         tma_load_3d(kd + kAtBoxBytes, &kmap, x0 + 64, j * kAtBN, b, &sh->k_full[st]);
       }
+      if (*abort) {  // let the copies this thread issued land before the CTA exits
+        mbar_wait_drain(&sh->q_full, 0, kDrainCycles);
+        for (int jj = max(0, j - 2); jj < j; ++jj)
+          mbar_wait_drain(&sh->k_full[jj & 1], (jj >> 1) & 1, kDrainCycles);
+      }
     } else if (warp == 10 && lane == 0) {
       // ------------------------------------------------ TMA: V ring
       prefetch_tmap(&vmap);
-      for (int j = 0; j < nt; ++j) {
+      int j = 0;
+      for (; j < nt; ++j) {
         const int st = j & 1;
         // stage st is free once P_{j-2}.V_{j-2} has finished
         if (!mbar_wait(&sh->p_empty[st], ((j >> 1) & 1) ^ 1, a.err, abort)) break;
@@ -189,6 +199,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         mbar_arrive_expect_tx(&sh->v_full[st], kAtTileBytes);
         tma_load_3d(vd, &vmap, x0, j * kAtBN, b, &sh->v_full[st]);
         tma_load_3d(vd + kAtBoxBytes, &vmap, x0 + 64, j * kAtBN, b, &sh->v_full[st]);
+      }
+      if (*abort) {
+        for (int jj = max(0, j - 2); jj < j; ++jj)
+          mbar_wait_drain(&sh->v_full[jj & 1], (jj >> 1) & 1, kDrainCycles);
       }
     } else if (warp == 9) {
       // ------------------------------------------------ MMA issuer
@@ -247,7 +261,12 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           if (j >= 1 && !(ok = issue_pv(j - 1))) break;
         }
         if (ok) ok = issue_pv(nt - 1);
-        if (ok) tc_commit(&sh->o_full);
+        if (ok) {
+          tc_commit(&sh->o_full);
+        } else {  // let the MMAs this thread issued finish before TMEM is freed
+          tc_commit(&sh->drain);
+          mbar_wait_drain(&sh->drain, 0, kDrainCycles);
+        }
       }
       __syncwarp();
     }

@@ -76,6 +76,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// Bounded wait that ignores the abort flag, for draining asynchronous copies
+// and MMAs still in flight before a CTA that gave up releases its memory.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity,
+                                                long long limit_cycles) {
+  const uint32_t a = smem_u32(bar);
+  const long long t0 = clock64();
+  while (!mbar_try_wait(a, parity))
+    if (clock64() - t0 > limit_cycles) return false;
+  return true;
+}
+
 // Warp-uniform variant: every lane waits, the warp proceeds only if all did.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err,
                                                volatile int* abort) {
@@ -145,21 +156,6 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tc_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// tcgen05.wait::ld that also names the 32 destination registers of an earlier
-// tcgen05.ld as in/out operands, so the compiler cannot move a use of them
-// above the wait (needed when a load is left in flight across other work).
-__device__ __forceinline__ void tc_wait_ld_regs(uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.wait::ld.sync.aligned;"
-      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
-        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
-        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
-        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-      :
-      : "memory");
 }
 
 // 32 lanes x 32 consecutive 32-bit columns; thread i gets its lane's columns.

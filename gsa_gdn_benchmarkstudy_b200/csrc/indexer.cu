@@ -41,6 +41,7 @@ constexpr int kIdxKBytes = kIdxBN * kIdxD * 2;    // 4 KB per stage
 constexpr int kIdxTmemCols = 256;                 // 2 buffers x 4 heads x 32
 constexpr int kIdxThreads = 192;                  // warps 0-3 epilogue, 4 TMA, 5 MMA
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr long long kIdxDrainCycles = 200000000LL;  // ~0.1 s after an abort
 
 struct IdxSmem {
   uint64_t q_full;
@@ -48,11 +49,13 @@ struct IdxSmem {
   uint64_t k_empty[kIdxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
+  uint64_t drain;  // MMAs in flight when the CTA gives up
   uint32_t tmem_base;
   int abort;
 };
 constexpr int kIdxSmemBytes =
     1024 /*align slack*/ + kIdxHeads * kIdxQBytes + kIdxStages * kIdxKBytes + 256;
+static_assert(sizeof(IdxSmem) <= 256, "control block exceeds its 256-byte slot");
 
 __global__ void __launch_bounds__(kIdxThreads, 2)
     indexer_tc_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -89,6 +92,7 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
       mbar_init(&sh->acc_full[s], 1);
       mbar_init(&sh->acc_empty[s], 4);
     }
+    mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
@@ -110,12 +114,18 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
       mbar_arrive_expect_tx(&sh->q_full, kIdxHeads * kIdxQBytes);
       for (int h = 0; h < kIdxHeads; ++h)
         tma_load_3d(q_s + h * kIdxQBytes, &qmap, h * kIdxD, row0, b, &sh->q_full);
-      for (int s = 0; s < nsub; ++s) {
+      int s = 0;
+      for (; s < nsub; ++s) {
         const int st = s % kIdxStages;
         const uint32_t ph = (s / kIdxStages) & 1;
         if (!mbar_wait(&sh->k_empty[st], ph ^ 1, a.err, abort)) break;
         mbar_arrive_expect_tx(&sh->k_full[st], kIdxKBytes);
         tma_load_3d(k_s + st * kIdxKBytes, &kmap, 0, key0 + s * kIdxBN, b, &sh->k_full[st]);
+      }
+      if (*abort) {  // let the copies this thread issued land before the CTA exits
+        mbar_wait_drain(&sh->q_full, 0, kIdxDrainCycles);
+        for (int ss = max(0, s - kIdxStages); ss < s; ++ss)
+          mbar_wait_drain(&sh->k_full[ss % kIdxStages], (ss / kIdxStages) & 1, kIdxDrainCycles);
       }
     }
   } else if (warp == 5) {
@@ -128,8 +138,8 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
       for (int s = 0; ok && s < nsub; ++s) {
         const int st = s % kIdxStages;
         const int buf = s & 1;
-        if (!mbar_wait(&sh->k_full[st], (s / kIdxStages) & 1, a.err, abort)) break;
-        if (!mbar_wait(&sh->acc_empty[buf], ((s >> 1) & 1) ^ 1, a.err, abort)) break;
+        if (!(ok = mbar_wait(&sh->k_full[st], (s / kIdxStages) & 1, a.err, abort))) break;
+        if (!(ok = mbar_wait(&sh->acc_empty[buf], ((s >> 1) & 1) ^ 1, a.err, abort))) break;
         tc_fence_after();
 #pragma unroll
         for (int h = 0; h < kIdxHeads; ++h) {
@@ -142,6 +152,10 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
         }
         tc_commit(&sh->k_empty[st]);
         tc_commit(&sh->acc_full[buf]);
+      }
+      if (!ok) {  // let the MMAs this thread issued finish before TMEM is freed
+        tc_commit(&sh->drain);
+        mbar_wait_drain(&sh->drain, 0, kIdxDrainCycles);
       }
     }
     __syncwarp();
