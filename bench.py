@@ -41,10 +41,13 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "GSA fwd tokens/s at D=2048,T=16K (1-8 B200); indexer TFLOP/s, sparse-attn GB/s"
 UNIT = "tokens/s"
-# dram__bytes_read.sum + dram__bytes_write.sum of one masked-attention launch
-# from the ncu capture summarised in profiles/ (None until captured).
-ATTN_TRAFFIC_BYTES_PER_LAUNCH = None
-ATTN_TRAFFIC_NOTE = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one masked-attention launch of
+# this bench at N=1, per config, from the ncu capture summarised in
+# profiles/masked_attn_cfg3_dram.md (306.33 MB read + 56.79 MB written).
+ATTN_TRAFFIC_BYTES_PER_LAUNCH = {"cfg3": 363_120_000}
+ATTN_TRAFFIC_NOTE = ("ncu capture of one launch at N=1 (profiles/masked_attn_cfg3_dram.md); "
+                     "algorithmic bytes per launch: q, k, v, og, out 64 MiB each + bitmask 32 MiB "
+                     "= 369 MB")
 
 
 def parse_args():
@@ -330,10 +333,11 @@ def run_ours(args, cfg, rank: int, world: int, device):
         achieved = flops / (attn_ms / 1e3) / 1e12
         peak = pk["bf16_tflops"]
         rl = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-              "frac": round(achieved / peak, 4), "traffic": ATTN_TRAFFIC_BYTES_PER_LAUNCH,
+              "frac": round(achieved / peak, 4),
+              "traffic": ATTN_TRAFFIC_BYTES_PER_LAUNCH.get(cfg.name) if world == 1 else None,
               "kernel": "masked_attn_kernel (tcgen05)", "peak_kind": f"bf16 burst, {pk['_source']}",
               "ms_per_launch": round(attn_ms, 4)}
-        if ATTN_TRAFFIC_NOTE:
+        if rl["traffic"] is not None:
             rl["traffic_note"] = ATTN_TRAFFIC_NOTE
     extra = {}
     if split:
