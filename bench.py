@@ -302,9 +302,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
         flush.zero_()
         e2e_ev[i][0].record(stream)
         if e2e_step is None:
-            xd = x_host.to(device, non_blocking=True)
-            out = model(xd)
-            out_host.copy_(out, non_blocking=True)
+            model.forward_host(x_host, out=out_host)  # copies overlapped with compute
         else:
             e2e_step()
         e2e_ev[i][1].record(stream)

@@ -408,3 +408,130 @@ class GatedSparseAttention(nn.Module):
             out = F.linear(attn.view(B, T, D), self.o_proj.weight)
         _nvtx_pop()
         return out
+
+    # ------------------------------------------------------- host-buffer forward
+    def forward_host(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     chunks: int = 5) -> torch.Tensor:
+        """Forward from host memory to host memory with the PCIe copies hidden.
+
+        For callers whose activations live in host memory.  ``x_host`` [B, T, D]
+        (pinned; pageable input is pinned first) is copied to the current device
+        in ``chunks`` pieces on a copy stream while earlier pieces compute, and
+        each piece of the output is copied back into ``out`` (a pinned [B, T, D]
+        host tensor, allocated if None) as soon as it is done.  Returns ``out``
+        after the copies have completed.
+
+        With B == 1 the pieces are blocks of query rows: attention is causal, so
+        rows [r0, r1) need only keys [0, r1), which earlier pieces have already
+        projected; the kernels take the block through ``q_pos0``.  The first and
+        last blocks are half the size of the others, since the first copy in and
+        the last copy out are the ones nothing overlaps.  With B > 1
+        the pieces are groups of whole sequences.  The result equals
+        ``forward`` up to the rounding of the projection GEMMs, which cuBLAS may
+        block differently for a smaller problem."""
+        if x_host.is_cuda:
+            raise RuntimeError("forward_host takes a host tensor; use forward for device tensors")
+        if x_host.dtype not in (torch.bfloat16, torch.float32):
+            raise RuntimeError(f"unsupported dtype {x_host.dtype}")
+        B, T, D = x_host.shape
+        dev = torch.device("cuda", torch.cuda.current_device())
+        x_host = x_host.contiguous()
+        if not x_host.is_pinned():
+            x_host = x_host.pin_memory()
+        if out is None:
+            out = torch.empty(B, T, D, dtype=x_host.dtype).pin_memory()
+        elif out.shape != (B, T, D) or out.dtype != x_host.dtype or out.is_cuda:
+            raise ValueError(f"out must be a host [{B}, {T}, {D}] {x_host.dtype} tensor")
+        compute = torch.cuda.current_stream(dev)
+        h2d, d2h = self._copy_streams(dev)
+        h2d.wait_stream(compute)  # device buffers below come from the compute stream's pool
+        if B > 1:
+            groups = max(1, min(chunks, B))
+            bounds = [B * i // groups for i in range(groups + 1)]
+            x_dev = torch.empty(B, T, D, device=dev, dtype=x_host.dtype)
+            for b0, b1 in zip(bounds[:-1], bounds[1:]):
+                with torch.cuda.stream(h2d):
+                    x_dev[b0:b1].copy_(x_host[b0:b1], non_blocking=True)
+                compute.wait_stream(h2d)
+                y = self.forward(x_dev[b0:b1])
+                d2h.wait_stream(compute)
+                with torch.cuda.stream(d2h):
+                    out[b0:b1].copy_(y, non_blocking=True)
+                y.record_stream(d2h)
+            compute.wait_stream(d2h)
+            d2h.synchronize()
+            return out
+        return self._forward_host_rows(x_host, out, chunks, dev, compute, h2d, d2h)
+
+    def _copy_streams(self, device: torch.device):
+        key = ("copy", device)
+        pair = self._streams.get(key)
+        if pair is None:
+            pair = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
+            self._streams[key] = pair
+        return pair
+
+    def _forward_host_rows(self, x_host, out, chunks, dev, compute, h2d, d2h):
+        """B == 1: row blocks [r0, r1) in sequence order, keys [0, r1) for each."""
+        _, T, D = x_host.shape
+        H = self.num_heads
+        tiles = (T + 127) // 128
+        n = max(1, min(chunks, tiles))
+        # block bounds on 128-row tiles: half-size first and last blocks
+        if n <= 2:
+            cuts = [tiles * i / n for i in range(n + 1)]
+        else:
+            unit = tiles / (n - 1)
+            cuts = [0.0] + [unit * (i - 0.5) for i in range(1, n)] + [float(tiles)]
+        bounds = sorted({min(T, 128 * int(round(c))) for c in cuts} | {0, T})
+        w, bias = self._get_fused_weight()
+        cos, sin = self.rotary_emb(T, dev, x_host.dtype)
+        x_dev = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
+        proj = torch.empty(1, T, self._proj_padded, device=dev, dtype=x_host.dtype)
+        q = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        attn = torch.empty_like(q)
+        y = torch.empty_like(q)
+        done_in = []
+        for r0, r1 in zip(bounds[:-1], bounds[1:]):
+            with torch.cuda.stream(h2d):
+                x_dev[:, r0:r1].copy_(x_host[:, r0:r1], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                done_in.append(e)
+        parts_all = self.split(proj)
+        side = self._side_stream(dev)
+        for c, (r0, r1) in enumerate(zip(bounds[:-1], bounds[1:])):
+            compute.wait_event(done_in[c])
+            with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
+                torch.addmm(bias, x_dev[0, r0:r1], w.t(), out=proj[0, r0:r1])
+            rows = {name: t[:, r0:r1] for name, t in parts_all.items()}
+            # indexer + top-k on the side stream beside RoPE + value gate, as in forward
+            side.wait_stream(compute)
+            with torch.cuda.stream(side):
+                sel = self.select_rows(rows, parts_all["ik"][:, :r1], q_pos0=r0, tkv=r1)
+            with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
+                ops.rope_gates(rows["q"], rows["k"], cos[r0:r1], sin[r0:r1], H,
+                               v_src=rows["v"], vg_src=rows["vg"],
+                               out=(q[:, r0:r1], k[:, r0:r1], v[:, r0:r1]))
+            compute.wait_stream(side)
+            if isinstance(sel, tuple):
+                for t in sel:
+                    t.record_stream(compute)
+            if torch.is_tensor(sel):
+                with _Stage(self, "k:masked_attention", "gsa_b200/sparse_attn"):
+                    ops.masked_attention(q[:, r0:r1], k[:, :r1], v[:, :r1], sel, self.scale, H,
+                                         og=rows["og"], q_pos0=r0, out=attn[:, r0:r1])
+            else:
+                attn[:, r0:r1] = self.attend_selected(rows, sel, k[:, :r1], v[:, :r1],
+                                                      q[:, r0:r1], q_pos0=r0)
+            with _Stage(self, "lib:o_proj", "gsa_b200/o_proj"):
+                torch.mm(attn[0, r0:r1], self.o_proj.weight.t(), out=y[0, r0:r1])
+            d2h.wait_stream(compute)
+            with torch.cuda.stream(d2h):
+                out[:, r0:r1].copy_(y[:, r0:r1], non_blocking=True)
+        y.record_stream(d2h)
+        compute.wait_stream(d2h)
+        d2h.synchronize()
+        return out

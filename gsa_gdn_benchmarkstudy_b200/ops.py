@@ -75,10 +75,11 @@ def indexer_topk_workspace_size(B: int, Tq: int, Tkv: int) -> int:
 # --------------------------------------------------------------------------- RoPE + G2
 def rope_gates(q_src: torch.Tensor, k_src: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                num_heads: int, v_src: torch.Tensor | None = None,
-               vg_src: torch.Tensor | None = None):
+               vg_src: torch.Tensor | None = None, out: tuple | None = None):
     """RoPE on q/k and (optionally) v * sigmoid(vg); all sources [B, T, H*d] with one row stride.
 
-    Returns (q, k, v) as contiguous [B, T, H*d] tensors (v is None without v_src)."""
+    Returns (q, k, v) as contiguous [B, T, H*d] tensors (v is None without v_src); ``out``
+    = (q, k, v) supplies them (contiguous, the sources' shape and dtype)."""
     _cuda(q_src, k_src, cos, sin, v_src, vg_src)
     B, T, W = q_src.shape
     d = W // num_heads
@@ -92,9 +93,19 @@ def rope_gates(q_src: torch.Tensor, k_src: torch.Tensor, cos: torch.Tensor, sin:
         raise ValueError(f"cos/sin must be [T, d] = [{T}, {d}]")
     cos = cos.to(q_src.dtype).contiguous()
     sin = sin.to(q_src.dtype).contiguous()
-    q = torch.empty(B, T, W, device=q_src.device, dtype=q_src.dtype)
-    k = torch.empty_like(q)
-    v = torch.empty_like(q) if v_src is not None else None
+    if out is None:
+        q = torch.empty(B, T, W, device=q_src.device, dtype=q_src.dtype)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q) if v_src is not None else None
+    else:
+        q, k, v = out
+        for t in (q, k) + ((v,) if v_src is not None else ()):
+            if (t is None or t.shape != (B, T, W) or t.dtype != q_src.dtype
+                    or not t.is_contiguous() or t.device != q_src.device):
+                raise ValueError(f"out tensors must be contiguous [{B}, {T}, {W}] "
+                                 f"{q_src.dtype} on the sources' device")
+        if v_src is None:
+            v = None
     rc = _lib.load().gsa_rope_gates(
         q_src.data_ptr(), k_src.data_ptr(),
         v_src.data_ptr() if v_src is not None else None,
