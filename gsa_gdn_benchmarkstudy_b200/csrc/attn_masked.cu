@@ -24,10 +24,10 @@
 //              budget to kSoftmaxRegs (setmaxnreg) so a whole 128-key row of S
 //              stays in registers.
 //   warp 8     TMA producer for Q and the K ring (2 stages)
-//   warp 9     TMEM owner + single-thread tcgen05.mma issuer
+//   warp 9     TMEM owner; one thread issues the QK^T tcgen05.mma
 //   warp 10    TMA producer for the V ring (2 stages), so K loads never queue
 //              behind V loads
-//   warp 11    idle (completes the third warpgroup for setmaxnreg)
+//   warp 11    one thread issues the P.V tcgen05.mma
 // Per key tile j (parity par = j % 2):
 //   softmax:  load the row of S_j from TMEM into registers and release the S
 //             buffer at once (the MMA warp then computes S_{j+2} into it while
@@ -39,8 +39,8 @@
 //             2^((m_old - m_new)*c).  P (bf16) goes to shared buffer par in the
 //             128B-swizzled K-major layout the MMA reads, once P.V of tile j-2
 //             (same buffer, same O_par) has finished.
-//   MMA:      S_{j+2} = Q.K_{j+2}^T as soon as S_j is released, then
-//             O_par += P_j.V_j once P_j is in shared memory.
+//   MMA:      S_{j+2} = Q.K_{j+2}^T as soon as S_j is released (warp 9), and
+//             O_par += P_j.V_j once P_j is in shared memory (warp 11).
 // Epilogue: M = max(m_even, m_odd), O = O_even*2^((m_even-M)c) + O_odd*2^((m_odd-M)c)
 //   (likewise l), o = O / l rounded to bf16; optional gate bf16(o * bf16(sigmoid(og))).
 //
@@ -77,7 +77,7 @@ struct AtSmem {
   uint64_t p_full[2];   // P_j written by the 4 softmax warps
   uint64_t p_empty[2];  // P_j.V_j finished (also: V stage and P buffer free)
   uint64_t o_full;
-  uint64_t drain;       // MMAs in flight when the CTA gives up
+  uint64_t drain[2];    // [issuer] MMAs in flight when the CTA gives up
   uint32_t tmem_base;
   int abort;
   float xm[2][kAtBM];  // [parity][row] running max, for the epilogue merge
@@ -148,7 +148,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_init(&sh->p_empty[s], 1);
     }
     mbar_init(&sh->o_full, 1);
-    mbar_init(&sh->drain, 1);
+    mbar_init(&sh->drain[0], 1);
+    mbar_init(&sh->drain[1], 1);
     sh->abort = 0;
     fence_mbar_init();
   }
@@ -204,21 +205,26 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         for (int jj = max(0, j - 2); jj < j; ++jj)
           mbar_wait_drain(&sh->v_full[jj & 1], (jj >> 1) & 1, kDrainCycles);
       }
-    } else if (warp == 9) {
-      // ------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        constexpr uint32_t idesc_s = idesc_bf16_f32(kAtBM, kAtBN, 0, 0);  // Q, K both K-major
-        constexpr uint32_t idesc_o = idesc_bf16_f32(kAtBM, kAtD, 0, 1);   // P K-major, V MN-major
+    } else if ((warp == 9 || warp == 11) && lane == 0) {
+      // ------------------------------------------------ MMA issuers
+      // Two threads issue: warp 9 the QK^T MMAs, warp 11 the P.V MMAs.  An
+      // issuing thread is held while its MMAs execute, so with one issuer every
+      // barrier wait between two batches left the tensor pipe idle.  The two
+      // streams touch disjoint TMEM (S buffers / O accumulators), and each
+      // thread's tcgen05.commit tracks only its own MMAs.
+      constexpr uint32_t idesc_s = idesc_bf16_f32(kAtBM, kAtBN, 0, 0);  // Q, K both K-major
+      constexpr uint32_t idesc_o = idesc_bf16_f32(kAtBM, kAtD, 0, 1);   // P K-major, V MN-major
+      bool ok = true;
+      if (warp == 9) {
         const uint32_t q_base = smem_u32(q_s);
         const uint32_t k_base = smem_u32(k_s);
-        const uint32_t v_base = smem_u32(v_s);
-        const uint32_t p_base = smem_u32(p_s);
-        bool ok = mbar_wait(&sh->q_full, 0, a.err, abort);
-
-        // S_j = Q.K_j^T into S buffer j%2 (free: S_{j-2} was loaded by the softmax)
-        auto issue_s = [&](int j) -> bool {
+        ok = mbar_wait(&sh->q_full, 0, a.err, abort);
+        // S_j = Q.K_j^T into S buffer j%2, once the softmax has loaded S_{j-2}
+        for (int j = 0; ok && j < nt; ++j) {
           const int st = j & 1;
-          if (!mbar_wait(&sh->k_full[st], (j >> 1) & 1, a.err, abort)) return false;
+          if (j >= 2 && !(ok = mbar_wait(&sh->s_empty[st], ((j - 2) >> 1) & 1, a.err, abort)))
+            break;
+          if (!(ok = mbar_wait(&sh->k_full[st], (j >> 1) & 1, a.err, abort))) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kAtD / 16; ++kk) {
@@ -228,14 +234,16 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             tc_mma_ss(tmem + st * kAtBN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
           }
           tc_commit(&sh->s_full[st]);
-          return true;
-        };
-        // O_par += P_j.V_j
-        auto issue_pv = [&](int j) -> bool {
+        }
+      } else {
+        const uint32_t v_base = smem_u32(v_s);
+        const uint32_t p_base = smem_u32(p_s);
+        // O_par += P_j.V_j once the softmax has written P_j
+        for (int j = 0; ok && j < nt; ++j) {
           const int st = j & 1;
           const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&sh->p_full[st], ph, a.err, abort)) return false;
-          if (!mbar_wait(&sh->v_full[st], ph, a.err, abort)) return false;
+          if (!(ok = mbar_wait(&sh->p_full[st], ph, a.err, abort))) break;
+          if (!(ok = mbar_wait(&sh->v_full[st], ph, a.err, abort))) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kAtBN / 16; ++kk) {
@@ -246,29 +254,14 @@ __global__ void __launch_bounds__(kAtThreads, 1)
             tc_mma_ss(tmem + (2 + st) * kAtBN, ad, bd, idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&sh->p_empty[st]);
-          return true;
-        };
-
-        if (ok) ok = issue_s(0);
-        if (ok && nt > 1) ok = issue_s(1);
-        // Expected event order: S_j released, then P_{j-1} written (the two
-        // parities run half a tile apart), so S_{j+2} goes first.
-        for (int j = 0; ok && j < nt; ++j) {
-          if (j + 2 < nt) {
-            ok = mbar_wait(&sh->s_empty[j & 1], (j >> 1) & 1, a.err, abort) && issue_s(j + 2);
-            if (!ok) break;
-          }
-          if (j >= 1 && !(ok = issue_pv(j - 1))) break;
         }
-        if (ok) ok = issue_pv(nt - 1);
-        if (ok) {
-          tc_commit(&sh->o_full);
-        } else {  // let the MMAs this thread issued finish before TMEM is freed
-          tc_commit(&sh->drain);
-          mbar_wait_drain(&sh->drain, 0, kDrainCycles);
-        }
+        if (ok) tc_commit(&sh->o_full);
       }
-      __syncwarp();
+      if (!ok) {  // let the MMAs this thread issued finish before TMEM is freed
+        uint64_t* d = &sh->drain[warp == 9 ? 0 : 1];
+        tc_commit(d);
+        mbar_wait_drain(d, 0, kDrainCycles);
+      }
     }
   } else {
     reg_alloc<kSoftmaxRegs>();
