@@ -45,20 +45,26 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// One try_wait with a suspend-time hint: a thread whose phase is not yet
+// complete sleeps in hardware until it completes (or kWaitSuspendNs passes)
+// instead of spinning, so waiting warps leave the issue slots of their SM
+// sub-partition to the warps that compute.
+constexpr uint32_t kWaitSuspendNs = 10000000u;  // 10 ms
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(addr), "r"(parity)
+      : "r"(addr), "r"(parity), "r"(kWaitSuspendNs)
       : "memory");
   return ok != 0;
 }
 
 // Waits for the phase of `bar` with the given parity.  Gives up after
-// kWaitLimitCycles, or as soon as another warp of the CTA raised *abort:
+// kWaitLimitCycles (checked between try_waits, each suspended for at most
+// kWaitSuspendNs), or as soon as another warp of the CTA raised *abort:
 // then records kDevErrTimeout in *err, raises *abort and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
                                           volatile int* abort) {
