@@ -314,9 +314,9 @@ def run_ours(args, cfg, rank: int, world: int, device):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = t.item() / args.steps
-    # bytes copied per step by rank 0: its input share in, the full output out
+    # bytes copied per step by each rank: its input share in, its output rows out
     h2d = x_host.numel() * x_host.element_size() // world
-    d2h = out_host.numel() * out_host.element_size()
+    d2h = out_host.numel() * out_host.element_size() // world
 
     if rank != 0:
         return

@@ -86,7 +86,9 @@ class ShardedGSA:
 
     ``local_input(x)`` picks this rank's share of a full input; ``__call__``
     takes that share (on this rank's GPU) and returns the FULL output on every
-    rank; ``forward_host(x_host)`` does the same from pinned host memory."""
+    rank.  ``forward_host(x_local_host)`` runs the same forward from this rank's
+    share in pinned host memory and returns this rank's rows of the output in
+    host memory (the whole output is the union of the ranks' returns)."""
 
     def __init__(self, model, group, T: int, B: int):
         self.model = model
@@ -118,11 +120,15 @@ class ShardedGSA:
 
     # ---------------------------------------------------------------- forward
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
-        if self.mode == "batch":
-            return gather_batch(self.model(x_local), self.group)
-        return self._forward_rows(x_local)
+        return self._forward(x_local, gather=True)
 
-    def _forward_rows(self, x_loc: torch.Tensor) -> torch.Tensor:
+    def _forward(self, x_local: torch.Tensor, gather: bool) -> torch.Tensor:
+        if self.mode == "batch":
+            y = self.model(x_local)
+            return gather_batch(y, self.group) if gather else y
+        return self._forward_rows(x_local, gather)
+
+    def _forward_rows(self, x_loc: torch.Tensor, gather: bool = True) -> torch.Tensor:
         m = self.model
         T, D, H = self.T, m.hidden_size, m.num_heads
         proj = m.project(x_loc)
@@ -145,14 +151,19 @@ class ShardedGSA:
             off += n
         attn = torch.cat(outs, dim=1)
         out_local = F.linear(attn, m.o_proj.weight)
-        return gather_rows(out_local, T, self.group)
+        return gather_rows(out_local, T, self.group) if gather else out_local
 
     def forward_host(self, x_local_host: torch.Tensor) -> torch.Tensor:
         """This rank's input share from pinned host memory -> device, sharded forward,
-        full output read back into a pinned host buffer (returned)."""
+        this rank's output rows read back into a pinned host buffer (returned).
+
+        Rows come back in the order of ``local_input`` (this rank's blocks, or
+        its sequences); no output all-gather is needed, so each rank copies
+        back 1/P of the output."""
         dev = torch.device("cuda", torch.cuda.current_device())
-        out = self(x_local_host.to(dev, non_blocking=True))
+        out = self._forward(x_local_host.to(dev, non_blocking=True), gather=False)
         if self._host_out is None or self._host_out.shape != out.shape:
             self._host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
         self._host_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
         return self._host_out

@@ -69,3 +69,17 @@ def test_batch_sharded_matches_unsharded(group):
     runner = ShardedGSA(m, group, T=cfg.T, B=cfg.B)
     got = runner(runner.local_input(x))
     assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("name", ["small_bf16", "tiny_bf16"])
+def test_forward_host_returns_this_ranks_rows(group, name):
+    """forward_host: pinned host share in, this rank's output rows out (in the
+    order of local_input), equal to those rows of the device-resident result."""
+    cfg = TEST_CONFIGS[name]
+    m = _model(cfg)
+    x = make_input(cfg)
+    runner = ShardedGSA(m, group, T=cfg.T, B=cfg.B)
+    full = runner(runner.local_input(x.cuda())).cpu()
+    got = runner.forward_host(runner.local_input(x).pin_memory())
+    assert not got.is_cuda
+    assert torch.equal(got, runner.local_input(full))
