@@ -5,8 +5,9 @@
 One step = one forward of the configuration's whole batch (default cfg3:
 B=1, T=16384, D=2048, H=16, k=2048, bf16) on synthetic seeded inputs and
 weights.  For N > 1 the driver launches one rank per GPU under torchrun; B=1
-configurations shard query rows zig-zag over the ranks (k_I/K/V and the output
-rows are all-gathered with NCCL), batched ones shard sequences.
+configurations shard query rows zig-zag over the ranks (k_I, K and V are
+all-gathered with NCCL; each rank keeps its own output rows), batched ones shard
+sequences.
 
 Rank 0 prints ONE JSON line.  ``value`` is whole-job tokens/s with inputs
 resident in HBM, timed per step with CUDA events (max over ranks), L2 flushed
@@ -240,7 +241,8 @@ def run_ours(args, cfg, rank: int, world: int, device):
         runner = ShardedGSA(model, dist.group.WORLD, T=cfg.T, B=cfg.B)
         x_local_host = runner.local_input(x_host).pin_memory()
         x_dev = x_local_host.to(device)
-        step = lambda: runner(x_dev)  # noqa: E731
+        # each rank keeps its own output rows: the job's output is their union
+        step = lambda: runner(x_dev, gather=False)  # noqa: E731
         e2e_step = lambda: runner.forward_host(x_local_host)  # noqa: E731
     else:
         x_dev = x_host.to(device)

@@ -119,8 +119,11 @@ class ShardedGSA:
         return self._pos
 
     # ---------------------------------------------------------------- forward
-    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
-        return self._forward(x_local, gather=True)
+    def __call__(self, x_local: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        """Sharded forward of this rank's share.  Returns the full output on every
+        rank, or with ``gather=False`` only this rank's rows (in the order of
+        ``local_input``), which skips the output all-gather."""
+        return self._forward(x_local, gather=gather)
 
     def _forward(self, x_local: torch.Tensor, gather: bool) -> torch.Tensor:
         if self.mode == "batch":
