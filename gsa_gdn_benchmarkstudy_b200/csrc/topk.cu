@@ -219,18 +219,30 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
           // 4. bits for higher bins, candidates of the threshold bin
           const int seg = ((nwords + kTopkWarps - 1) / kTopkWarps) * 32;
           const int s0 = min(warp * seg, nwords * 32), s1 = min(s0 + seg, nwords * 32);
-          for (int j0 = s0; j0 < s1; j0 += 32) {
-            const int j = j0 + lane;
-            const uint32_t u = j < n ? key_at(j) : kNegInfKey;
-            const bool fin = u != kNegInfKey;
-            const int bn = fin ? bin_of(u) : -1;
-            const uint32_t hib = __ballot_sync(0xFFFFFFFFu, bn > bstar);
-            if (bn == bstar) {
-              const int c = atomicAdd(&sh.n_cand, 1);
-              sh.cand_key[c] = u;
-              sh.cand_idx[c] = j;
+          // four 32-key groups per step: their loads are in flight together
+          constexpr int G = 4;
+          for (int jb = s0; jb < s1; jb += G * 32) {
+            uint32_t ug[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              const int j = jb + g * 32 + lane;
+              ug[g] = (j < n && jb + g * 32 < s1) ? key_at(j) : kNegInfKey;
             }
-            if (lane == 0) sh.bits[j0 >> 5] = hib;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              const int j0 = jb + g * 32;
+              if (j0 >= s1) break;
+              const int j = j0 + lane;
+              const uint32_t u = ug[g];
+              const int bn = u != kNegInfKey ? bin_of(u) : -1;
+              const uint32_t hib = __ballot_sync(0xFFFFFFFFu, bn > bstar);
+              if (bn == bstar) {
+                const int c = atomicAdd(&sh.n_cand, 1);
+                sh.cand_key[c] = u;
+                sh.cand_idx[c] = j;
+              }
+              if (lane == 0) sh.bits[j0 >> 5] = hib;
+            }
           }
           __syncthreads();
           // 5. exact rank among the candidates: (key desc, index asc)
