@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-rows", type=int, default=256)
+    ap.add_argument("--adaptive-k", action="store_true",
+                    help="opt-in variance-based k per row (not the reference module's fixed k)")
     return ap.parse_args()
 
 
@@ -211,11 +213,11 @@ def run_reference(args, cfg, rank: int):
 
 
 # ─────────────────────────────────────────────────────────────── our arm
-def build_model(cfg, device):
+def build_model(cfg, device, adaptive_k: bool = False):
     from gsa_gdn_benchmarkstudy_b200 import GatedSparseAttention
     from gsa_gdn_benchmarkstudy_b200.workloads import init_weights_
 
-    m = GatedSparseAttention(**cfg.module_kwargs())
+    m = GatedSparseAttention(**cfg.module_kwargs(), adaptive_k=adaptive_k)
     init_weights_(m, seed=1)
     m = m.to(cfg.torch_dtype).to(device).eval()
     m.fuse_projections()
@@ -233,7 +235,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
         dist.barrier()
     _lib.load()
     torch.set_grad_enabled(False)
-    model = build_model(cfg, device)
+    model = build_model(cfg, device, args.adaptive_k)
     x_host = make_input(cfg).pin_memory()
 
     if world > 1:
@@ -359,7 +361,8 @@ def run_ours(args, cfg, rank: int, world: int, device):
                    "global_batch": cfg.B, "seq_len": cfg.T,
                    "parallelism": ("single GPU" if world == 1 else
                                    ("query-row zig-zag shards" if cfg.B == 1 else "batch shards")),
-                   "l2": "flushed between steps (256 MB memset outside the step events)"},
+                   "l2": "flushed between steps (256 MB memset outside the step events)",
+                   **({"adaptive_k": True} if args.adaptive_k else {})},
         "gpu_launches": own_launches,
         "clocks": clocks.summary(),
         "e2e": {"value": round(cfg.B * cfg.T / (e2e_ms / 1e3), 1), "unit": UNIT,

@@ -51,6 +51,19 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _i64, _vp],
     ),
+    "gsa_row_variance": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "gsa_adaptive_k_width": (_i32, [_i32, _i32]),
+    "gsa_topk_select_adaptive": (
+        _i32,
+        [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _vp,
+         _vp, _i64, _vp],
+    ),
+    "gsa_indexer_topk_adaptive_workspace_size": (_i64, [_i32, _i32, _i32]),
+    "gsa_indexer_topk_adaptive": (
+        _i32,
+        [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _f32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+         _i32, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp],
+    ),
     "gsa_masked_attention": (
         _i32,
         [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _f32, _i32, _i32,

@@ -207,8 +207,26 @@ int indexer_topk_impl(const void* q, int64_t q_stride, const void* k, int64_t k_
   int rc = indexer_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
                         q_pos0, H_I, d_I, scores, stride, 0, s);
   if (rc) return rc;
-  return finish(gsa::launch_topk(scores, stride, B, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
-                                 bitmask_words, s));
+  return finish(gsa::launch_topk(scores, stride, B, Tq, Tkv, q_pos0, k_sel, k_sel,
+                                 gsa::AdaptiveK{}, indices, mask, bitmask, bitmask_words, s));
+}
+
+// Adaptive-k workspace: the score rows, then row_var [B*Tq] floats, then the
+// double var_sum on a 16-byte boundary.
+int64_t adaptive_var_offset(int B, int Tq, int Tkv) {
+  return static_cast<int64_t>(B) * Tq * score_row_stride(Tkv) * static_cast<int64_t>(sizeof(float));
+}
+int64_t adaptive_sum_offset(int B, int Tq, int Tkv) {
+  const int64_t end = adaptive_var_offset(B, Tq, Tkv) +
+                      static_cast<int64_t>(B) * Tq * static_cast<int64_t>(sizeof(float));
+  return (end + 15) / 16 * 16;
+}
+
+int check_adaptive_k(int k_base, int k_min, int k_max) {
+  if (k_base < 0 || k_min < 0 || k_max < 1 || k_min > k_max)
+    return set_error(GSA_ERR_INVALID_ARG, "adaptive k needs k_base >= 0, 0 <= k_min <= k_max, "
+                                          "k_max >= 1");
+  return GSA_OK;
 }
 
 }  // namespace
@@ -351,8 +369,98 @@ int gsa_topk_select(const float* scores, int64_t score_stride, int B, int Tq, in
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
-  return finish(gsa::launch_topk(scores, score_stride, B, Tq, Tkv, q_pos0, k_sel, indices, mask,
-                                 bitmask, bitmask_words, static_cast<cudaStream_t>(stream)));
+  return finish(gsa::launch_topk(scores, score_stride, B, Tq, Tkv, q_pos0, k_sel, k_sel,
+                                 gsa::AdaptiveK{}, indices, mask, bitmask, bitmask_words,
+                                 static_cast<cudaStream_t>(stream)));
+}
+
+int gsa_row_variance(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                     int q_pos0, float* row_var, double* var_sum, void* stream) {
+  if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0) return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (!row_var || !var_sum) return set_error(GSA_ERR_INVALID_ARG, "row_var / var_sum is NULL");
+  if (reinterpret_cast<uintptr_t>(var_sum) % alignof(double))
+    return set_error(GSA_ERR_ALIGNMENT, "var_sum must be 8-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (B == 0 || Tq == 0) return finish(cudaMemsetAsync(var_sum, 0, sizeof(double), s));
+  if (!scores) return set_error(GSA_ERR_INVALID_ARG, "scores is NULL");
+  if (score_stride < Tkv) return set_error(GSA_ERR_INVALID_ARG, "score_stride < Tkv");
+  return finish(gsa::launch_row_variance(scores, score_stride, B, Tq, Tkv, q_pos0, row_var,
+                                         var_sum, s));
+}
+
+int gsa_topk_select_adaptive(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                             int q_pos0, int k_base, int k_min, int k_max, const float* row_var,
+                             const double* var_sum, int64_t var_rows, int32_t* row_k,
+                             int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                             int64_t bitmask_words, void* stream) {
+  if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0) return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  int rc = check_adaptive_k(k_base, k_min, k_max);
+  if (rc) return rc;
+  if (B == 0 || Tq == 0) return GSA_OK;
+  if (!scores || !row_var || !var_sum)
+    return set_error(GSA_ERR_INVALID_ARG, "scores / row_var / var_sum is NULL");
+  if (var_rows < 1) return set_error(GSA_ERR_INVALID_ARG, "var_rows < 1");
+  if (score_stride < Tkv) return set_error(GSA_ERR_INVALID_ARG, "score_stride < Tkv");
+  if (bitmask && bitmask_words < gsa_bitmask_words(Tkv))
+    return set_error(GSA_ERR_INVALID_ARG, "bitmask_words < gsa_bitmask_words(Tkv)");
+  DeviceState* st = nullptr;
+  rc = device_state(&st);
+  if (rc) return rc;
+  gsa::AdaptiveK ad;
+  ad.row_var = row_var;
+  ad.var_sum = var_sum;
+  ad.var_rows = var_rows;
+  ad.k_base = k_base;
+  ad.k_min = k_min;
+  ad.k_max = k_max;
+  ad.row_k = row_k;
+  const int width = gsa_adaptive_k_width(k_max, Tkv);
+  return finish(gsa::launch_topk(scores, score_stride, B, Tq, Tkv, q_pos0, 0, width, ad, indices,
+                                 mask, bitmask, bitmask_words, static_cast<cudaStream_t>(stream)));
+}
+
+int gsa_adaptive_k_width(int k_max, int Tkv) { return k_max < Tkv ? k_max : Tkv; }
+
+int64_t gsa_indexer_topk_adaptive_workspace_size(int B, int Tq, int Tkv) {
+  if (B <= 0 || Tq <= 0 || Tkv <= 0) return 0;
+  return adaptive_sum_offset(B, Tq, Tkv) + 16;
+}
+
+int gsa_indexer_topk_adaptive(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                              const void* w, int64_t w_stride, const float* bias, float scale,
+                              int dtype, int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                              int k_base, int k_min, int k_max, void* workspace,
+                              int64_t workspace_bytes, int32_t* row_k, int32_t* indices,
+                              uint8_t* mask, uint32_t* bitmask, int64_t bitmask_words,
+                              void* stream) {
+  if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0) return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  int rc = check_adaptive_k(k_base, k_min, k_max);
+  if (rc) return rc;
+  if (B == 0 || Tq == 0) return GSA_OK;
+  if (!workspace) return set_error(GSA_ERR_INVALID_ARG, "workspace is NULL");
+  if (workspace_bytes < gsa_indexer_topk_adaptive_workspace_size(B, Tq, Tkv))
+    return set_error(GSA_ERR_INVALID_ARG,
+                     "workspace smaller than gsa_indexer_topk_adaptive_workspace_size");
+  if (!aligned16(workspace)) return set_error(GSA_ERR_ALIGNMENT, "workspace not 16-byte aligned");
+  if (bitmask && bitmask_words < gsa_bitmask_words(Tkv))
+    return set_error(GSA_ERR_INVALID_ARG, "bitmask_words < gsa_bitmask_words(Tkv)");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* base = static_cast<char*>(workspace);
+  float* scores = reinterpret_cast<float*>(base);
+  float* row_var = reinterpret_cast<float*>(base + adaptive_var_offset(B, Tq, Tkv));
+  double* var_sum = reinterpret_cast<double*>(base + adaptive_sum_offset(B, Tq, Tkv));
+  const int64_t stride = score_row_stride(Tkv);
+  rc = indexer_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv, q_pos0,
+                    H_I, d_I, scores, stride, 0, s);
+  if (rc) return rc;
+  rc = gsa_row_variance(scores, stride, B, Tq, Tkv, q_pos0, row_var, var_sum, stream);
+  if (rc) return rc;
+  return gsa_topk_select_adaptive(scores, stride, B, Tq, Tkv, q_pos0, k_base, k_min, k_max,
+                                  row_var, var_sum, static_cast<int64_t>(B) * Tq, row_k, indices,
+                                  mask, bitmask, bitmask_words, stream);
 }
 
 int gsa_masked_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,

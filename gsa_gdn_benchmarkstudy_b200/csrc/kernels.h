@@ -40,9 +40,29 @@ cudaError_t launch_indexer_simt(const void* q, int64_t q_stride, const void* k, 
 cudaError_t launch_fill_upper(float* out, int64_t out_stride, int B, int Tq, int Tkv, int q_pos0,
                               cudaStream_t stream);
 
+// Variance-based per-row k (adaptive mode).  k_row = clamp(floor(k_base *
+// max(var_sum / var_rows, 1e-6) / max(row_var[row], 1e-6)), k_min, k_max).
+// row_var == nullptr selects the fixed k of launch_topk's k_sel.
+struct AdaptiveK {
+  const float* row_var = nullptr;   // [B * Tq]
+  const double* var_sum = nullptr;  // sum of row_var over all rows of the batch
+  int64_t var_rows = 0;             // number of rows var_sum covers
+  int k_base = 0, k_min = 0, k_max = 0;
+  int32_t* row_k = nullptr;         // optional [B * Tq] output of k_row
+};
+
+// indices / mask rows are k_width slots wide (k_width >= the k of any row).
 cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
-                        int q_pos0, int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                        int q_pos0, int k_sel, int k_width, const AdaptiveK& ad,
+                        int32_t* indices, uint8_t* mask, uint32_t* bitmask,
                         int64_t bitmask_words, cudaStream_t stream);
+
+// Per-row population variance of the finite scores among columns
+// [0, min(q_pos0 + r + 1, Tkv)) into row_var[B * Tq], and their sum over all
+// rows (summed in a fixed order, so repeat calls give the same bits) into
+// *var_sum.
+cudaError_t launch_row_variance(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                                int q_pos0, float* row_var, double* var_sum, cudaStream_t stream);
 
 struct MaskedAttnArgs {
   const uint32_t* bitmask;

@@ -38,8 +38,11 @@ constexpr int kDigitBits = 11;
 constexpr int kCandCap = 1024;  // candidate list capacity
 constexpr int kMaxWords = 2048; // bitmask words held in shared memory (Tkv <= 65536)
 
+// -0.0 maps to the key of +0.0: the two compare equal (as in torch.topk), so
+// they tie and the lower column index wins.
 __device__ __forceinline__ uint32_t ord_key(float f) {
-  const uint32_t x = __float_as_uint(f);
+  const uint32_t x0 = __float_as_uint(f);
+  const uint32_t x = x0 == 0x80000000u ? 0u : x0;
   return (x & 0x80000000u) ? ~x : (x | 0x80000000u);
 }
 // ord_key(-inf) (0xFF800000 inverted): below every finite key.
@@ -123,10 +126,26 @@ __device__ __forceinline__ void find_threshold_bin(TopkShared& sh, int krem) {
   __syncthreads();
 }
 
+// k of one row in adaptive mode (gsa_explained.ipynb, "Adaptive Top-K" cell):
+//   avg_var = mean over the batch's rows of row_var, clamped to >= 1e-6
+//   k = clamp(floor(k_base * avg_var / max(row_var, 1e-6)), k_min, k_max)
+// in fp32 with round-to-nearest multiply and divide, as torch computes it.
+// A NaN row variance gives k_max.
+__device__ __forceinline__ int adaptive_row_k(const AdaptiveK& ad, int64_t row) {
+  const float avg =
+      fmaxf(static_cast<float>(*ad.var_sum / static_cast<double>(ad.var_rows)), 1e-6f);
+  const float t = __fdiv_rn(__fmul_rn(static_cast<float>(ad.k_base), avg),
+                            fmaxf(ad.row_var[row], 1e-6f));
+  float kf = floorf(t);
+  kf = fmaxf(kf, static_cast<float>(ad.k_min));
+  kf = fminf(kf, static_cast<float>(ad.k_max));
+  return static_cast<int>(kf);
+}
+
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
-    const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0, int k_sel,
-    int32_t* __restrict__ indices, uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask,
-    int64_t bm_words) {
+    const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
+    int k_fixed, int k_width, AdaptiveK ad, int32_t* __restrict__ indices,
+    uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask, int64_t bm_words) {
   __shared__ TopkShared sh;
 
   const int tid = threadIdx.x;
@@ -137,13 +156,25 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   const int r = static_cast<int>(row % Tq);
   const int n = min(q_pos0 + r + 1, Tkv);
   const float* srow = scores + row * score_stride;
-  int32_t* irow = indices ? indices + row * k_sel : nullptr;
-  uint8_t* mrow = mask ? mask + row * k_sel : nullptr;
+  int32_t* irow = indices ? indices + row * k_width : nullptr;
+  uint8_t* mrow = mask ? mask + row * k_width : nullptr;
   uint32_t* brow = bitmask ? bitmask + row * bm_words : nullptr;
   const bool vec_ok = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0;
   const int nwords = (n + 31) / 32;
+  const int k_sel = ad.row_var ? adaptive_row_k(ad, row) : k_fixed;
+  if (ad.row_k && tid == 0) ad.row_k[row] = k_sel;
 
   auto key_at = [&](int j) -> uint32_t { return ord_key(__ldg(srow + j)); };
+
+  if (k_sel <= 0) {  // nothing selected: an all-zero bitmask and masked slots
+    if (brow)
+      for (int64_t w = tid; w < bm_words; w += kTopkThreads) brow[w] = 0u;
+    for (int s = tid; s < k_width; s += kTopkThreads) {
+      if (irow) irow[s] = min(s, Tkv - 1);
+      if (mrow) mrow[s] = 0;
+    }
+    return;
+  }
 
   // =================================================================== fast path
   bool done = false;
@@ -302,7 +333,14 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     }
     __syncthreads();
   }
-  if (done) return;
+  if (done) {
+    // adaptive rows narrower than the output (k_sel < k_width): masked filler
+    for (int s = k_sel + tid; s < k_width; s += kTopkThreads) {
+      if (irow) irow[s] = min(s, Tkv - 1);
+      if (mrow) mrow[s] = 0;
+    }
+    return;
+  }
 
   // =================================================================== exact path
   uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
@@ -455,23 +493,130 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   if (brow) {
     for (int64_t wd = span / 32 + tid; wd < bm_words; wd += kTopkThreads) brow[wd] = 0u;
   }
-  // filler slots after the selected ones (n < k_sel): future positions, masked
+  // filler slots after the selected ones (n < k_width): future positions, masked
   const int n_sel = min(n, k_sel);
-  for (int s = n_sel + tid; s < k_sel; s += kTopkThreads) {
+  for (int s = n_sel + tid; s < k_width; s += kTopkThreads) {
     if (irow) irow[s] = min(s, Tkv - 1);
     if (mrow) mrow[s] = 0;
   }
 }
 
+// ------------------------------------------------------------ row variance
+// Adaptive mode's statistics (gsa_explained.ipynb, "Adaptive Top-K" cell):
+// over the row's valid (finite-or-NaN, i.e. != -inf) scores,
+//   mean = sum / max(count, 1),  var = sum((s - mean)^2) / max(count, 1).
+// Two passes over the row (the second mostly from L2), block sums in a fixed
+// order.
+
+constexpr int kVarThreads = 256;
+constexpr int kSumThreads = 1024;
+
+__device__ __forceinline__ float block_sum_f(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kVarThreads / 32; ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kVarThreads) row_variance_kernel(
+    const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
+    float* __restrict__ row_var) {
+  __shared__ float red[kVarThreads / 32];
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int r = static_cast<int>(row % Tq);
+  const int n = min(q_pos0 + r + 1, Tkv);
+  const float* srow = scores + row * score_stride;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0;
+  const int nv = vec_ok ? (n >> 2) : 0;
+  const float4* s4 = reinterpret_cast<const float4*>(srow);
+  const float kNegInf = -__int_as_float(0x7F800000);
+
+  float sum = 0.f, cnt = 0.f;
+  auto acc1 = [&](float f) {
+    if (f != kNegInf) {
+      sum += f;
+      cnt += 1.f;
+    }
+  };
+  for (int v = tid; v < nv; v += kVarThreads) {
+    const float4 f = __ldg(s4 + v);
+    acc1(f.x);
+    acc1(f.y);
+    acc1(f.z);
+    acc1(f.w);
+  }
+  for (int j = 4 * nv + tid; j < n; j += kVarThreads) acc1(__ldg(srow + j));
+  sum = block_sum_f(sum, red);
+  cnt = block_sum_f(cnt, red);
+  const float c = fmaxf(cnt, 1.f);
+  const float mean = __fdiv_rn(sum, c);
+
+  float m2 = 0.f;
+  auto acc2 = [&](float f) {
+    if (f != kNegInf) {
+      const float d = f - mean;
+      m2 = fmaf(d, d, m2);
+    }
+  };
+  for (int v = tid; v < nv; v += kVarThreads) {
+    const float4 f = __ldg(s4 + v);
+    acc2(f.x);
+    acc2(f.y);
+    acc2(f.z);
+    acc2(f.w);
+  }
+  for (int j = 4 * nv + tid; j < n; j += kVarThreads) acc2(__ldg(srow + j));
+  m2 = block_sum_f(m2, red);
+  if (tid == 0) row_var[row] = __fdiv_rn(m2, c);
+}
+
+// One CTA: sum of row_var[0, rows) in double, each thread a strided slice,
+// then a fixed tree.
+__global__ void __launch_bounds__(kSumThreads) var_sum_kernel(const float* __restrict__ row_var,
+                                                              int64_t rows,
+                                                              double* __restrict__ var_sum) {
+  __shared__ double part[kSumThreads];
+  double a = 0.0;
+  for (int64_t i = threadIdx.x; i < rows; i += kSumThreads) a += static_cast<double>(row_var[i]);
+  part[threadIdx.x] = a;
+  __syncthreads();
+  for (int h = kSumThreads / 2; h > 0; h >>= 1) {
+    if (static_cast<int>(threadIdx.x) < h) part[threadIdx.x] += part[threadIdx.x + h];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *var_sum = part[0];
+}
+
 }  // namespace
 
 cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
-                        int q_pos0, int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                        int q_pos0, int k_sel, int k_width, const AdaptiveK& ad,
+                        int32_t* indices, uint8_t* mask, uint32_t* bitmask,
                         int64_t bitmask_words, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * Tq;
   if (rows == 0) return cudaSuccess;
   topk_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-      scores, score_stride, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask, bitmask_words);
+      scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
+      bitmask_words);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_row_variance(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                                int q_pos0, float* row_var, double* var_sum, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(B) * Tq;
+  if (rows == 0) return cudaSuccess;
+  row_variance_kernel<<<static_cast<unsigned>(rows), kVarThreads, 0, stream>>>(
+      scores, score_stride, Tq, Tkv, q_pos0, row_var);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  var_sum_kernel<<<1, kSumThreads, 0, stream>>>(row_var, rows, var_sum);
   return cudaGetLastError();
 }
 

@@ -159,19 +159,37 @@ class AdaptiveTopKSelector(nn.Module):
     ``forward(scores)`` returns (indices int64 [B,T,k], mask bool [B,T,k], k_eff).
     Indices come back in ascending order (the order gsa_opt.py:674-677 sorts
     into); valid slots precede masked filler slots; ties go to the lower index.
-    ``k_min`` is stored for interface parity; the reference never reads it."""
+    In the default mode ``k_min`` is stored for interface parity; the
+    reference never reads it.
 
-    def __init__(self, k_base: int = 2048, k_min: int = 256, k_max: int = 4096):
+    ``adaptive=True`` (opt-in; not part of the reference module) gives each row
+    its own k by the variance rule of the reference's notebook
+    (gsa_explained.ipynb:575-592): k_r = clamp(floor(k_base * mean_var /
+    max(var_r, 1e-6)), k_min, k_max), var_r the variance of row r's valid
+    scores and mean_var their mean over the batch (clamped to >= 1e-6).
+    ``forward`` then returns (indices int64 [B,T,min(k_max,T_kv)], mask, k per
+    row as an int64 [B,T] tensor)."""
+
+    def __init__(self, k_base: int = 2048, k_min: int = 256, k_max: int = 4096,
+                 adaptive: bool = False):
         super().__init__()
         self.k_base = k_base
         self.k_min = k_min
         self.k_max = k_max
+        self.adaptive = adaptive
 
     def k_effective(self, t_kv: int) -> int:
         return min(self.k_base, self.k_max, t_kv)
 
     def forward(self, scores: torch.Tensor):
         B, T, T_kv = scores.shape
+        if self.adaptive:
+            sc = scores.float().contiguous()
+            row_var, var_sum = ops.row_variance(sc, q_pos0=T_kv)
+            idx, mask, _, row_k = ops.topk_select_adaptive(
+                sc, self.k_base, self.k_min, self.k_max, row_var, var_sum, B * T,
+                q_pos0=T_kv, want_bitmask=False)
+            return idx.long(), mask, row_k.long()
         k_eff = self.k_effective(T_kv)
         # Every column is a candidate; -inf scores rank last and come back
         # with mask False, whatever the pattern of -inf in the rows.
@@ -215,7 +233,7 @@ class GatedSparseAttention(nn.Module):
 
     def __init__(self, hidden_size: int, num_heads: int, k_max: int = 4096,
                  d_indexer: int = 64, n_idx_heads: int = 4, k_base: int = 2048,
-                 k_min: int = 256):
+                 k_min: int = 256, adaptive_k: bool = False):
         super().__init__()
         self.hidden_size = hidden_size
         self.num_heads = num_heads
@@ -228,7 +246,9 @@ class GatedSparseAttention(nn.Module):
         self.o_proj = nn.Linear(hidden_size, hidden_size, bias=False)
 
         self.indexer = GatedLightningIndexer(hidden_size, d_indexer, n_idx_heads)
-        self.topk_selector = AdaptiveTopKSelector(k_base, k_min, k_max)
+        # adaptive_k (opt-in, no state): per-row k by the variance rule of
+        # AdaptiveTopKSelector(adaptive=True); the default is the reference's fixed k.
+        self.topk_selector = AdaptiveTopKSelector(k_base, k_min, k_max, adaptive=adaptive_k)
         self.value_gate = ValueGate(hidden_size)
         self.output_gate = OutputGate(hidden_size)
         self.rotary_emb = RotaryEmbedding(self.d_head)
@@ -237,7 +257,7 @@ class GatedSparseAttention(nn.Module):
         self._fused_bias: Optional[torch.Tensor] = None
         self._stage_events: Optional[list] = None
         self._streams: dict = {}
-        self._workspaces: dict = {}  # (device, stream) -> indexer/top-k scratch
+        self._workspaces: dict = {}  # (device, stream, slot) -> indexer/top-k scratch
         D, hi, di = hidden_size, n_idx_heads, d_indexer
         # Column layout of the fused projection output (gsa_opt.py:562-571 order).
         self._proj_sizes = [D, D, D, D, D, hi * di, di, hi]
@@ -307,16 +327,69 @@ class GatedSparseAttention(nn.Module):
         Returns the selection: a bitmask [B, Tq, W] for the tensor-core attention
         (bf16, d_head = 128), else (indices, mask) for the index-gather path."""
         Tkv = ik_all.shape[1] if tkv is None else tkv
-        k_eff = self.topk_selector.k_effective(Tkv)
         bf16_tc = parts["iq"].dtype == torch.bfloat16 and self.d_head == 128
         B, Tq = parts["iq"].shape[:2]
-        ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc)
+        sel = self.topk_selector
+        if sel.adaptive:
+            need = ops.indexer_topk_adaptive_workspace_size(B, Tq, Tkv)
+            ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc, need)
+            with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=4):
+                idx, mask, bitmask, _ = ops.indexer_topk_adaptive(
+                    parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale,
+                    sel.k_base, sel.k_min, sel.k_max, q_pos0=q_pos0, tkv=Tkv,
+                    want_indices=not bf16_tc, want_mask=not bf16_tc, want_bitmask=bf16_tc,
+                    workspace=ws, bitmask_out=bm)
+            return bitmask if bf16_tc else (idx, mask)
+        k_eff = sel.k_effective(Tkv)
+        ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc,
+                               ops.indexer_topk_workspace_size(B, Tq, Tkv))
         with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
             idx, mask, bitmask = ops.indexer_topk(
                 parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
                 q_pos0=q_pos0, tkv=Tkv, want_indices=not bf16_tc, want_mask=not bf16_tc,
                 want_bitmask=bf16_tc, workspace=ws, bitmask_out=bm)
         return bitmask if bf16_tc else (idx, mask)
+
+    def select_blocks(self, blocks, var_reduce=None, var_rows: Optional[int] = None) -> list:
+        """Selections for several blocks of query rows: ``blocks`` is a list of
+        (parts, ik_all, q_pos0, tkv) as ``select_rows`` takes them.
+
+        With a fixed k the blocks are independent.  With adaptive k every row's
+        k depends on the mean row variance of the whole batch, so all blocks'
+        scores and variances are computed first, their variance sums added,
+        ``var_reduce(total)`` (e.g. an all-reduce over the ranks holding the rest
+        of the batch) applied in place, and the blocks selected with
+        ``var_rows`` rows in the mean (default: the blocks' own rows)."""
+        sel = self.topk_selector
+        if not sel.adaptive or (len(blocks) == 1 and var_reduce is None):
+            return [self.select_rows(p, ik, q0, tkv) for p, ik, q0, tkv in blocks]
+        staged, total, rows = [], None, 0
+        for slot, (p, ik, q0, tkv) in enumerate(blocks):
+            B, Tq = p["iq"].shape[:2]
+            bf16_tc = p["iq"].dtype == torch.bfloat16 and self.d_head == 128
+            need = ops.indexer_topk_adaptive_workspace_size(B, Tq, tkv)
+            ws, bm = self._scratch(p["iq"].device, B, Tq, tkv, bf16_tc, need, slot=slot)
+            scores, row_var, var_sum = ops.adaptive_workspace_views(ws, B, Tq, tkv)
+            with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=3):
+                ops.indexer_scores(p["iq"], ik, p["iw"], self.indexer.idx_bias,
+                                   self.indexer.scale, q_pos0=q0, tkv=tkv, fill_upper=False,
+                                   out=scores)
+                ops.row_variance(scores[:, :, :tkv], q_pos0=q0, out=(row_var, var_sum))
+            total = var_sum.clone() if total is None else total + var_sum
+            rows += B * Tq
+            staged.append((scores[:, :, :tkv], row_var, q0, bf16_tc, bm))
+        if var_reduce is not None:
+            var_reduce(total)
+        out = []
+        for scores, row_var, q0, bf16_tc, bm in staged:
+            with _Stage(self, "k:topk_adaptive", "gsa_b200/indexer_topk"):
+                idx, mask, bitmask, _ = ops.topk_select_adaptive(
+                    scores, sel.k_base, sel.k_min, sel.k_max, row_var, total,
+                    var_rows if var_rows is not None else rows, q_pos0=q0,
+                    want_indices=not bf16_tc, want_mask=not bf16_tc, want_bitmask=bf16_tc,
+                    bitmask_out=bm)
+            out.append(bitmask if bf16_tc else (idx, mask))
+        return out
 
     def attend_selected(self, parts: dict, selection, k_all: torch.Tensor, v_all: torch.Tensor,
                         q_rows: torch.Tensor, q_pos0: int) -> torch.Tensor:
@@ -346,9 +419,11 @@ class GatedSparseAttention(nn.Module):
         sel = self.select_rows(parts, ik_all, q_pos0, tkv=k_all.shape[1])
         return self.attend_selected(parts, sel, k_all, v_all, q_rows, q_pos0)
 
-    def _scratch(self, device: torch.device, B: int, Tq: int, Tkv: int, want_bitmask: bool):
-        """Score scratch and selection bitmask for indexer + top-k, kept per
-        (device, current stream).
+    def _scratch(self, device: torch.device, B: int, Tq: int, Tkv: int, want_bitmask: bool,
+                 need: int, slot: int = 0):
+        """Score scratch (``need`` bytes) and selection bitmask for indexer + top-k,
+        kept per (device, current stream, slot); blocks whose selections must
+        coexist use different slots.
 
         Reusing them keeps a 1 GiB-scale allocation (T=16K) out of every
         forward.  Work on one stream runs in order, so a later call cannot
@@ -356,8 +431,7 @@ class GatedSparseAttention(nn.Module):
         the attention of the same forward; a later selection on the side
         stream waits for that attention (``side.wait_stream(main)`` at the top
         of ``forward``), and ``attend_rows`` selects and attends on one stream."""
-        need = ops.indexer_topk_workspace_size(B, Tq, Tkv)
-        key = (device, torch.cuda.current_stream(device).cuda_stream)
+        key = (device, torch.cuda.current_stream(device).cuda_stream, slot)
         ws, bm = self._workspaces.get(key, (None, None))
         if ws is None or ws.numel() < need:
             ws = torch.empty(need, dtype=torch.uint8, device=device)
@@ -377,6 +451,13 @@ class GatedSparseAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
                 ) -> torch.Tensor:
+        return self._forward_impl(x)
+
+    def _forward_impl(self, x: torch.Tensor, var_reduce=None,
+                      var_rows: Optional[int] = None) -> torch.Tensor:
+        """``forward``; ``var_reduce`` / ``var_rows`` as in ``select_blocks`` let a
+        caller whose batch spans several processes average adaptive k's row
+        variances over all of it."""
         if not x.is_cuda:
             raise RuntimeError("gsa_b200.GatedSparseAttention runs on CUDA only (no CPU path)")
         if x.dtype not in (torch.bfloat16, torch.float32):
@@ -395,7 +476,7 @@ class GatedSparseAttention(nn.Module):
         side = self._side_stream(x.device)
         side.wait_stream(main)
         with torch.cuda.stream(side):
-            sel = self.select_rows(parts, parts["ik"], q_pos0=0)
+            sel = self.select_blocks([(parts, parts["ik"], 0, T)], var_reduce, var_rows)[0]
         with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
             q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, self.num_heads,
                                      v_src=parts["v"], vg_src=parts["vg"])
@@ -445,8 +526,10 @@ class GatedSparseAttention(nn.Module):
         compute = torch.cuda.current_stream(dev)
         h2d, d2h = self._copy_streams(dev)
         h2d.wait_stream(compute)  # device buffers below come from the compute stream's pool
-        if B > 1:
-            groups = max(1, min(chunks, B))
+        adaptive = self.topk_selector.adaptive
+        if B > 1 or adaptive:
+            # adaptive k averages row variances over the whole batch: one piece
+            groups = 1 if adaptive else max(1, min(chunks, B))
             bounds = [B * i // groups for i in range(groups + 1)]
             x_dev = torch.empty(B, T, D, device=dev, dtype=x_host.dtype)
             for b0, b1 in zip(bounds[:-1], bounds[1:]):

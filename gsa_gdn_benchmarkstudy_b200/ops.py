@@ -171,34 +171,25 @@ def fused_gated_indexer(q_idx, k_idx, w, bias, scale: float, causal: bool = True
     return s.contiguous() if s.stride(1) != Tkv else s
 
 
-def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
-                 scale: float, k_sel: int, q_pos0: int = 0, tkv: int | None = None,
-                 want_indices: bool = False, want_mask: bool = False, want_bitmask: bool = True,
-                 workspace: torch.Tensor | None = None, bitmask_out: torch.Tensor | None = None):
-    """Indexer + top-k in one C call; the scores live only in a scratch workspace.
-
-    Same inputs as ``indexer_scores``; outputs as ``topk_select``
-    (indices int32, mask bool, bitmask int32 words), unrequested ones None.
-    ``bitmask_out`` (int32 [B, Tq, bitmask_words(Tkv)], contiguous) receives the
-    bitmask instead of a new tensor."""
+def _indexer_inputs(q_idx, k_idx, w, bias):
+    """Checked [B, Tq, H_I*d_I] view of q_idx, row strides, fp32 bias and dtype code."""
     _cuda(q_idx, k_idx, w, bias)
     B, Tq, H_I, d_I = q_idx.shape
     if q_idx.stride(3) != 1 or q_idx.stride(2) != d_I:
         q_idx = q_idx.contiguous()
     q3 = q_idx.as_strided((B, Tq, H_I * d_I), (q_idx.stride(0), q_idx.stride(1), 1))
-    Tkv = k_idx.shape[1] if tkv is None else tkv
     code = _dtype_code(q_idx)
     if k_idx.dtype != q_idx.dtype or w.dtype != q_idx.dtype:
         raise ValueError("q_idx, k_idx and w must share a dtype")
     qs, ks, ws = _rows(q3, H_I * d_I, "q_idx"), _rows(k_idx, d_I, "k_idx"), _rows(w, H_I, "w")
     bias32 = bias.detach().to(torch.float32).contiguous()
-    lib = _lib.load()
-    need = int(lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv))
-    if workspace is None or workspace.numel() * workspace.element_size() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=q_idx.device)
-    dev = q_idx.device
-    idx = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.int32) if want_indices else None
-    msk = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.uint8) if want_mask else None
+    return q3, qs, ks, ws, bias32, code, (B, Tq, H_I, d_I)
+
+
+def _selection_outputs(dev, B: int, Tq: int, width: int, Tkv: int, want_indices: bool,
+                       want_mask: bool, want_bitmask: bool, bitmask_out=None):
+    idx = torch.empty(B, Tq, width, device=dev, dtype=torch.int32) if want_indices else None
+    msk = torch.empty(B, Tq, width, device=dev, dtype=torch.uint8) if want_mask else None
     W = bitmask_words(Tkv)
     bm = None
     if want_bitmask:
@@ -210,14 +201,145 @@ def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias
             bm = bitmask_out
         else:
             bm = torch.empty(B, Tq, W, device=dev, dtype=torch.int32)
+    return idx, msk, bm, W
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _workspace(workspace, need: int, dev):
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    return workspace
+
+
+def indexer_topk(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor, bias: torch.Tensor,
+                 scale: float, k_sel: int, q_pos0: int = 0, tkv: int | None = None,
+                 want_indices: bool = False, want_mask: bool = False, want_bitmask: bool = True,
+                 workspace: torch.Tensor | None = None, bitmask_out: torch.Tensor | None = None):
+    """Indexer + top-k in one C call; the scores live only in a scratch workspace.
+
+    Same inputs as ``indexer_scores``; outputs as ``topk_select``
+    (indices int32, mask bool, bitmask int32 words), unrequested ones None.
+    ``bitmask_out`` (int32 [B, Tq, bitmask_words(Tkv)], contiguous) receives the
+    bitmask instead of a new tensor."""
+    q3, qs, ks, ws, bias32, code, (B, Tq, H_I, d_I) = _indexer_inputs(q_idx, k_idx, w, bias)
+    Tkv = k_idx.shape[1] if tkv is None else tkv
+    lib = _lib.load()
+    workspace = _workspace(workspace, int(lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv)),
+                           q_idx.device)
+    idx, msk, bm, W = _selection_outputs(q_idx.device, B, Tq, k_sel, Tkv, want_indices,
+                                         want_mask, want_bitmask, bitmask_out)
     rc = lib.gsa_indexer_topk(
         q3.data_ptr(), qs, k_idx.data_ptr(), ks, w.data_ptr(), ws, bias32.data_ptr(), float(scale),
         code, B, Tq, Tkv, int(q_pos0), H_I, d_I, int(k_sel), workspace.data_ptr(),
-        workspace.numel() * workspace.element_size(),
-        idx.data_ptr() if idx is not None else None, msk.data_ptr() if msk is not None else None,
-        bm.data_ptr() if bm is not None else None, W, _stream())
+        workspace.numel() * workspace.element_size(), _ptr(idx), _ptr(msk), _ptr(bm), W,
+        _stream())
     _lib.check(rc, "gsa_indexer_topk")
     return idx, (msk.bool() if msk is not None else None), bm
+
+
+# --------------------------------------------------------------------------- adaptive k
+def adaptive_k_width(k_max: int, tkv: int) -> int:
+    """Slots per row of adaptive-mode index / mask outputs: min(k_max, Tkv)."""
+    return int(_lib.load().gsa_adaptive_k_width(int(k_max), int(tkv)))
+
+
+def indexer_topk_adaptive_workspace_size(B: int, Tq: int, Tkv: int) -> int:
+    return int(_lib.load().gsa_indexer_topk_adaptive_workspace_size(int(B), int(Tq), int(Tkv)))
+
+
+def adaptive_workspace_views(workspace: torch.Tensor, B: int, Tq: int, Tkv: int):
+    """(scores [B, Tq, stride] fp32, row_var [B, Tq] fp32, var_sum [1] fp64) inside a
+    uint8 workspace of ``indexer_topk_adaptive_workspace_size`` bytes, laid out as
+    the C call lays it out."""
+    stride = (Tkv + 3) // 4 * 4
+    n_scores = B * Tq * stride * 4
+    sum_off = (n_scores + B * Tq * 4 + 15) // 16 * 16
+    scores = workspace[:n_scores].view(torch.float32).view(B, Tq, stride)
+    row_var = workspace[n_scores:n_scores + B * Tq * 4].view(torch.float32).view(B, Tq)
+    var_sum = workspace[sum_off:sum_off + 8].view(torch.float64)
+    return scores, row_var, var_sum
+
+
+def indexer_topk_adaptive(q_idx: torch.Tensor, k_idx: torch.Tensor, w: torch.Tensor,
+                          bias: torch.Tensor, scale: float, k_base: int, k_min: int, k_max: int,
+                          q_pos0: int = 0, tkv: int | None = None, want_indices: bool = False,
+                          want_mask: bool = False, want_bitmask: bool = True,
+                          workspace: torch.Tensor | None = None,
+                          bitmask_out: torch.Tensor | None = None):
+    """``indexer_topk`` with the per-row adaptive k, averaged over the call's rows.
+
+    Returns (indices [B,Tq,adaptive_k_width], mask, bitmask, row_k int32 [B,Tq])."""
+    q3, qs, ks, ws, bias32, code, (B, Tq, H_I, d_I) = _indexer_inputs(q_idx, k_idx, w, bias)
+    Tkv = k_idx.shape[1] if tkv is None else tkv
+    lib = _lib.load()
+    workspace = _workspace(workspace, indexer_topk_adaptive_workspace_size(B, Tq, Tkv),
+                           q_idx.device)
+    width = adaptive_k_width(k_max, Tkv)
+    idx, msk, bm, W = _selection_outputs(q_idx.device, B, Tq, width, Tkv, want_indices,
+                                         want_mask, want_bitmask, bitmask_out)
+    row_k = torch.empty(B, Tq, device=q_idx.device, dtype=torch.int32)
+    rc = lib.gsa_indexer_topk_adaptive(
+        q3.data_ptr(), qs, k_idx.data_ptr(), ks, w.data_ptr(), ws, bias32.data_ptr(), float(scale),
+        code, B, Tq, Tkv, int(q_pos0), H_I, d_I, int(k_base), int(k_min), int(k_max),
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(), row_k.data_ptr(),
+        _ptr(idx), _ptr(msk), _ptr(bm), W, _stream())
+    _lib.check(rc, "gsa_indexer_topk_adaptive")
+    return idx, (msk.bool() if msk is not None else None), bm, row_k
+
+
+def _check_scores(scores: torch.Tensor):
+    _cuda(scores)
+    if scores.dtype != torch.float32 or scores.dim() != 3 or scores.stride(2) != 1:
+        raise ValueError("scores must be float32 [B, Tq, Tkv] with unit inner stride")
+    B, Tq, Tkv = scores.shape
+    if B > 1 and scores.stride(0) != Tq * scores.stride(1):
+        raise ValueError("scores batch stride must equal Tq * row stride")
+    return B, Tq, Tkv
+
+
+def row_variance(scores: torch.Tensor, q_pos0: int = 0, out=None):
+    """Per-row variance of the valid (!= -inf) causal scores and its sum over the rows.
+
+    Returns (row_var fp32 [B, Tq], var_sum fp64 [1]); ``out`` may supply that pair."""
+    B, Tq, Tkv = _check_scores(scores)
+    if out is None:
+        row_var = torch.empty(B, Tq, device=scores.device, dtype=torch.float32)
+        var_sum = torch.empty(1, device=scores.device, dtype=torch.float64)
+    else:
+        row_var, var_sum = out
+    rc = _lib.load().gsa_row_variance(scores.data_ptr(), scores.stride(1), B, Tq, Tkv,
+                                      int(q_pos0), row_var.data_ptr(), var_sum.data_ptr(),
+                                      _stream())
+    _lib.check(rc, "gsa_row_variance")
+    return row_var, var_sum
+
+
+def topk_select_adaptive(scores: torch.Tensor, k_base: int, k_min: int, k_max: int,
+                         row_var: torch.Tensor, var_sum: torch.Tensor, var_rows: int,
+                         q_pos0: int = 0, want_indices: bool = True, want_mask: bool = True,
+                         want_bitmask: bool = True, bitmask_out: torch.Tensor | None = None):
+    """Top-k with k per row from the row variances (``row_variance``); ``var_sum`` /
+    ``var_rows`` give the batch mean of the variances (summed over every row block
+    and rank of the batch).  Returns (indices, mask, bitmask, row_k int32 [B, Tq])."""
+    B, Tq, Tkv = _check_scores(scores)
+    _cuda(row_var, var_sum)
+    if row_var.dtype != torch.float32 or row_var.numel() != B * Tq or not row_var.is_contiguous():
+        raise ValueError("row_var must be a contiguous float32 tensor of B*Tq elements")
+    if var_sum.dtype != torch.float64 or var_sum.numel() != 1:
+        raise ValueError("var_sum must be a one-element float64 tensor")
+    width = adaptive_k_width(k_max, Tkv)
+    idx, msk, bm, W = _selection_outputs(scores.device, B, Tq, width, Tkv, want_indices,
+                                         want_mask, want_bitmask, bitmask_out)
+    row_k = torch.empty(B, Tq, device=scores.device, dtype=torch.int32)
+    rc = _lib.load().gsa_topk_select_adaptive(
+        scores.data_ptr(), scores.stride(1), B, Tq, Tkv, int(q_pos0), int(k_base), int(k_min),
+        int(k_max), row_var.data_ptr(), var_sum.data_ptr(), int(var_rows), row_k.data_ptr(),
+        _ptr(idx), _ptr(msk), _ptr(bm), W, _stream())
+    _lib.check(rc, "gsa_topk_select_adaptive")
+    return idx, (msk.bool() if msk is not None else None), bm, row_k
 
 
 # --------------------------------------------------------------------------- top-k
@@ -227,21 +349,12 @@ def topk_select(scores: torch.Tensor, k_sel: int, q_pos0: int = 0, want_indices:
 
     Returns (indices int32 [B,Tq,k] ascending + masked filler, mask bool [B,Tq,k],
     bitmask int32-storage uint32 words [B,Tq,W]); unrequested outputs are None."""
-    _cuda(scores)
-    if scores.dtype != torch.float32 or scores.dim() != 3 or scores.stride(2) != 1:
-        raise ValueError("scores must be float32 [B, Tq, Tkv] with unit inner stride")
-    B, Tq, Tkv = scores.shape
-    if B > 1 and scores.stride(0) != Tq * scores.stride(1):
-        raise ValueError("scores batch stride must equal Tq * row stride")
-    dev = scores.device
-    idx = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.int32) if want_indices else None
-    msk = torch.empty(B, Tq, k_sel, device=dev, dtype=torch.uint8) if want_mask else None
-    W = bitmask_words(Tkv)
-    bm = torch.empty(B, Tq, W, device=dev, dtype=torch.int32) if want_bitmask else None
+    B, Tq, Tkv = _check_scores(scores)
+    idx, msk, bm, W = _selection_outputs(scores.device, B, Tq, k_sel, Tkv, want_indices,
+                                         want_mask, want_bitmask)
     rc = _lib.load().gsa_topk_select(
         scores.data_ptr(), scores.stride(1), B, Tq, Tkv, int(q_pos0), int(k_sel),
-        idx.data_ptr() if idx is not None else None, msk.data_ptr() if msk is not None else None,
-        bm.data_ptr() if bm is not None else None, W, _stream())
+        _ptr(idx), _ptr(msk), _ptr(bm), W, _stream())
     _lib.check(rc, "gsa_topk_select")
     return idx, (msk.bool() if msk is not None else None), bm
 

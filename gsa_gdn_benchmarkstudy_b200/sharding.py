@@ -125,9 +125,17 @@ class ShardedGSA:
         ``local_input``), which skips the output all-gather."""
         return self._forward(x_local, gather=gather)
 
+    def _sum_over_ranks(self, t: torch.Tensor) -> None:
+        """In-place sum over the group: adaptive k's row-variance total."""
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
     def _forward(self, x_local: torch.Tensor, gather: bool) -> torch.Tensor:
         if self.mode == "batch":
-            y = self.model(x_local)
+            if self.model.topk_selector.adaptive:
+                y = self.model._forward_impl(x_local, var_reduce=self._sum_over_ranks,
+                                             var_rows=self.B * self.T)
+            else:
+                y = self.model(x_local)
             return gather_batch(y, self.group) if gather else y
         return self._forward_rows(x_local, gather)
 
@@ -145,13 +153,23 @@ class ShardedGSA:
         k_full = gather_rows(k, T, self.group)
         v_full = gather_rows(v, T, self.group)
         ik_full = gather_rows(parts["ik"].contiguous(), T, self.group)
-        outs, off = [], 0
+        outs, blocks, off = [], [], 0
         for s, e in self.blocks:
             n = e - s
             pb = {key: parts[key][:, off:off + n] for key in ("iq", "iw", "og")}
-            outs.append(m.attend_rows(pb, k_full[:, :e], v_full[:, :e], ik_full[:, :e],
-                                      q[:, off:off + n], q_pos0=s))
+            blocks.append((pb, s, e, off, n))
             off += n
+        if m.topk_selector.adaptive:
+            # every row's k needs the mean row variance over all ranks' rows
+            sels = m.select_blocks([(pb, ik_full[:, :e], s, e) for pb, s, e, _, _ in blocks],
+                                   var_reduce=self._sum_over_ranks, var_rows=self.B * T)
+            for (pb, s, e, o, n), sel in zip(blocks, sels):
+                outs.append(m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e],
+                                              q[:, o:o + n], q_pos0=s))
+        else:
+            for pb, s, e, o, n in blocks:
+                outs.append(m.attend_rows(pb, k_full[:, :e], v_full[:, :e], ik_full[:, :e],
+                                          q[:, o:o + n], q_pos0=s))
         attn = torch.cat(outs, dim=1)
         out_local = F.linear(attn, m.o_proj.weight)
         return gather_rows(out_local, T, self.group) if gather else out_local

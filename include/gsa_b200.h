@@ -122,7 +122,8 @@ GSA_API int gsa_indexer_scores(const void* q, int64_t q_stride,
  *
  * Row r has n = min(q_pos0 + r + 1, Tkv) valid scores (columns 0..n-1).
  * If n <= k_sel all valid columns are selected, otherwise the k_sel largest,
- * ties broken toward the lower column index.  Outputs (each may be NULL):
+ * ties (equal scores; -0.0 equals +0.0) broken toward the lower column
+ * index.  Outputs (each may be NULL):
  *   indices [B, Tq, k_sel] int32: selected columns in ascending order, then
  *           (k_sel - selected) filler slots holding future positions
  *           min(n + s, Tkv - 1) with mask 0 (the reference's -inf slots)
@@ -135,6 +136,68 @@ GSA_API int gsa_topk_select(const float* scores, int64_t score_stride,
                     int B, int Tq, int Tkv, int q_pos0, int k_sel,
                     int32_t* indices, uint8_t* mask,
                     uint32_t* bitmask, int64_t bitmask_words, void* stream);
+
+/*
+ * Adaptive k (opt-in; the reference module's selector always uses the fixed
+ * k above).  The rule is the variance-based one of the reference's tutorial
+ * notebook, gsa_explained.ipynb:575-592 ("Adaptive Top-K: How It Works"):
+ *   var_r   = population variance of row r's valid scores (!= -inf) among
+ *             columns [0, min(q_pos0 + r + 1, Tkv))
+ *   avg_var = max(sum_r var_r / var_rows, 1e-6)    (mean over the batch)
+ *   k_r     = clamp(floor(k_base * avg_var / max(var_r, 1e-6)), k_min, k_max)
+ * and row r then selects its k_r largest scores as gsa_topk_select does.
+ *
+ * gsa_row_variance writes var_r to row_var [B*Tq] and the sum over the call's
+ * rows to *var_sum (one double, 8-byte aligned; summed in a fixed order, so
+ * the same inputs give the same bits).  A caller whose batch spans several
+ * calls (row blocks, or ranks of a process group) adds their var_sum values
+ * before selecting, and passes the total row count as var_rows.
+ */
+GSA_API int gsa_row_variance(const float* scores, int64_t score_stride,
+                             int B, int Tq, int Tkv, int q_pos0,
+                             float* row_var, double* var_sum, void* stream);
+
+/* Slots per row of the index / mask outputs in adaptive mode:
+ * min(k_max, Tkv).  No row selects more. */
+GSA_API int gsa_adaptive_k_width(int k_max, int Tkv);
+
+/*
+ * Top-k selection with the per-row k_r above (replaces
+ * AdaptiveTopKSelector.forward, gsa_ref.py:138-150, in adaptive mode).
+ * Outputs as gsa_topk_select with rows gsa_adaptive_k_width(k_max, Tkv) slots
+ * wide: the selected columns ascending, then masked filler.  row_k
+ * [B*Tq] int32 (may be NULL) receives k_r.  Needs k_base >= 0,
+ * 0 <= k_min <= k_max, k_max >= 1, var_rows >= 1.  A row whose k_r is 0
+ * selects nothing.
+ */
+GSA_API int gsa_topk_select_adaptive(const float* scores, int64_t score_stride,
+                                     int B, int Tq, int Tkv, int q_pos0,
+                                     int k_base, int k_min, int k_max,
+                                     const float* row_var, const double* var_sum,
+                                     int64_t var_rows, int32_t* row_k,
+                                     int32_t* indices, uint8_t* mask,
+                                     uint32_t* bitmask, int64_t bitmask_words,
+                                     void* stream);
+
+/* Bytes of scratch gsa_indexer_topk_adaptive needs: the score rows of
+ * gsa_indexer_topk_workspace_size plus the row variances and their sum. */
+GSA_API int64_t gsa_indexer_topk_adaptive_workspace_size(int B, int Tq, int Tkv);
+
+/*
+ * gsa_indexer_topk in adaptive mode: indexer scores, gsa_row_variance over
+ * the call's B*Tq rows (var_rows = B*Tq), gsa_topk_select_adaptive.  The
+ * workspace (16-byte aligned) holds the scores, row variances and their sum.
+ */
+GSA_API int gsa_indexer_topk_adaptive(const void* q, int64_t q_stride,
+                                      const void* k, int64_t k_stride,
+                                      const void* w, int64_t w_stride,
+                                      const float* bias, float scale, int dtype,
+                                      int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I,
+                                      int k_base, int k_min, int k_max,
+                                      void* workspace, int64_t workspace_bytes,
+                                      int32_t* row_k, int32_t* indices, uint8_t* mask,
+                                      uint32_t* bitmask, int64_t bitmask_words,
+                                      void* stream);
 
 /* Number of uint32 words per row that gsa_topk_select / gsa_masked_attention
  * expect for a key range of Tkv. */

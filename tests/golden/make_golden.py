@@ -69,10 +69,73 @@ def stages(ref, m, x, rows=None):
     return dict(q=q, k=k, v=v, scores=scores, idx=idx, mask=mask, attn=attn, out=out, k_eff=k_eff)
 
 
+def notebook_adaptive_k(reference: Path, scores: torch.Tensor, k_base: int, k_min: int,
+                        k_max: int):
+    """Runs the adaptive-k cell of the reference's notebook (gsa_explained.ipynb:575-592)
+    on ``scores`` with its k_base / k_min / k_max set to the given values.
+
+    The cell's own source is executed; only its three parameter assignments are
+    replaced and its printing is discarded.  Returns (k_adaptive, variance)."""
+    import contextlib
+    import io
+    import json
+    import re
+    nb = json.loads((reference / "gsa_explained.ipynb").read_text())
+    cells = ["".join(c["source"]) for c in nb["cells"] if c["cell_type"] == "code"]
+    src = next(c for c in cells if "k_adaptive = (k_base" in c)
+    for name, val in (("k_base", k_base), ("k_min", k_min), ("k_max", k_max)):
+        src, n = re.subn(rf"^{name} = \d+", f"{name} = {val}", src, count=1, flags=re.M)
+        assert n == 1, name
+    ns = {"torch": torch, "final_scores": scores, "T": scores.shape[1]}
+    with contextlib.redirect_stdout(io.StringIO()):
+        exec(compile(src, "gsa_explained.ipynb[adaptive-k cell]", "exec"), ns)
+    return ns["k_adaptive"], ns["variance"]
+
+
+def adaptive_edge_scores() -> torch.Tensor:
+    """Seeded causal scores with the cases adaptive k must handle: a constant
+    row (variance 0 -> the 1e-6 clamp), exact ties, rows with few valid
+    scores and scattered -inf entries below the diagonal."""
+    g = torch.Generator().manual_seed(7)
+    B, T = 2, 96
+    s = torch.randn(B, T, T, generator=g) * 2.0
+    s[0, 40] = 0.25                                  # constant row
+    s[1, 50, :30] = s[1, 50, 0]                      # tied block
+    s[1, 60] = torch.round(s[1, 60] * 2) / 2         # many exact ties
+    drop = torch.rand(B, T, T, generator=g) < 0.1
+    s = s.masked_fill(drop, float("-inf"))           # scattered -inf
+    causal = torch.triu(torch.ones(T, T, dtype=torch.bool), diagonal=1)
+    return s.masked_fill(causal, float("-inf"))
+
+
+ADAPTIVE_PARAMS = ((48, 16, 4096), (4, 2, 6), (32, 0, 64), (2048, 256, 4096))
+
+
+def make_adaptive(reference: Path) -> None:
+    """Adaptive-k fixture: the notebook cell's k and variance on the tiny
+    configurations' reference scores and on the edge-case scores."""
+    inputs = {"edge": adaptive_edge_scores()}
+    for name in ("tiny_bf16", "tiny_fp32"):
+        inputs[name] = torch.load(HERE / f"{name}.pt")["scores"].float()
+    cases = []
+    for name, scores in inputs.items():
+        for kb, kmn, kmx in ADAPTIVE_PARAMS:
+            k_ad, var = notebook_adaptive_k(reference, scores, kb, kmn, kmx)
+            cases.append(dict(scores=name, k_base=kb, k_min=kmn, k_max=kmx,
+                              k=k_ad.to(torch.int32), variance=var))
+    torch.save(dict(edge_scores=inputs["edge"], cases=cases), HERE / "adaptive_k.pt")
+    print("adaptive_k saved:", len(cases), "cases")
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--parts", default="all", choices=("all", "adaptive"),
+                    help="'adaptive' regenerates only adaptive_k.pt (needs the tiny fixtures)")
     args = ap.parse_args()
+    if args.parts == "adaptive":
+        make_adaptive(Path(args.reference))
+        return 0
     sys.path.insert(0, str(Path(args.reference) / "gsa_triton"))
     import gsa_ref as ref  # the reference implementation, unmodified
     torch.set_grad_enabled(False)
@@ -121,6 +184,8 @@ def main() -> int:
               mask=st["mask"][:, r].contiguous())
     torch.save(fx, HERE / "cfg2_rows.pt")
     print("cfg2 saved")
+
+    make_adaptive(Path(args.reference))
     return 0
 
 

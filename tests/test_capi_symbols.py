@@ -58,3 +58,21 @@ def test_argument_checks_run_before_any_device_work(lib):
     # empty work is a no-op success
     assert lib.gsa_indexer_scores(None, 0, None, 0, None, 0, None, 1.0, 0, 0, 4, 4, 0, 4, 64,
                                   None, 4, 0, None) == 0
+
+
+def test_adaptive_k_entry_points_on_the_host(lib):
+    assert lib.gsa_adaptive_k_width(4096, 160) == 160
+    assert lib.gsa_adaptive_k_width(64, 160) == 64
+    # scores 1*4 rows * 8 floats = 128 B, row_var 16 B, var_sum on a 16 B boundary
+    assert lib.gsa_indexer_topk_adaptive_workspace_size(1, 4, 5) == 160
+    assert lib.gsa_indexer_topk_adaptive_workspace_size(0, 4, 5) == 0
+    # k_min > k_max and k_max < 1 are rejected before any device work
+    rc = lib.gsa_topk_select_adaptive(None, 8, 1, 1, 8, 0, 4, 9, 8, None, None, 1, None, None,
+                                      None, None, 0, None)
+    assert rc == 1 and b"k_min <= k_max" in lib.gsa_last_error_string()
+    rc = lib.gsa_indexer_topk_adaptive(None, 0, None, 0, None, 0, None, 1.0, 0, 1, 1, 8, 0, 4,
+                                       64, 4, 0, 0, None, 0, None, None, None, None, 0, None)
+    assert rc == 1
+    rc = lib.gsa_row_variance(None, 8, 1, 1, 8, 0, None, None, None)
+    assert rc == 1
+

@@ -216,6 +216,23 @@ def test_topk_edge_cases(T, k, ties, Tq, q_pos0):
     assert torch.equal(_bitmask_to_dense(bm, T), dense)
 
 
+@pytest.mark.parametrize("T,k", [(300, 40), (5000, 2048)])
+def test_topk_signed_zeros_tie(T, k):
+    """-0.0 and +0.0 compare equal (as in torch), so they tie and the lower
+    column wins whatever their signs; both the fast and the exact path."""
+    g = _gen(T + k)
+    s = torch.randint(-2, 3, (1, 8, T), generator=g).float()
+    s = torch.where((s == 0) & (torch.rand(1, 8, T, generator=g) < 0.5), torch.tensor(-0.0), s)
+    assert bool(torch.signbit(s[s == 0]).any()) and bool((~torch.signbit(s[s == 0])).any())
+    q_pos0 = T - 8
+    pos = torch.arange(q_pos0, T).view(1, 8, 1)
+    s = s.masked_fill(torch.arange(T).view(1, 1, T) > pos, NEG)
+    idx, mask, bm = ops.topk_select(s.cuda(), k, q_pos0=q_pos0)
+    si, sm = O.topk_select_stable(s, k)
+    assert torch.equal(idx.cpu().long(), si)
+    assert torch.equal(mask.cpu(), sm)
+
+
 def test_topk_module_api_handles_arbitrary_neg_inf():
     from gsa_gdn_benchmarkstudy_b200 import AdaptiveTopKSelector
     g = _gen(9)

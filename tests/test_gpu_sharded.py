@@ -36,8 +36,8 @@ def group():
     dist.destroy_process_group()
 
 
-def _model(cfg):
-    m = GatedSparseAttention(**cfg.module_kwargs())
+def _model(cfg, adaptive=False):
+    m = GatedSparseAttention(**cfg.module_kwargs(), adaptive_k=adaptive)
     init_weights_(m, seed=1)
     m = m.to(cfg.torch_dtype).cuda().eval()
     m.fuse_projections()
@@ -83,3 +83,23 @@ def test_forward_host_returns_this_ranks_rows(group, name):
     got = runner.forward_host(runner.local_input(x).pin_memory())
     assert not got.is_cuda
     assert torch.equal(got, runner.local_input(full))
+
+
+@pytest.mark.parametrize("name", ["small_bf16", "tiny_bf16"])
+def test_adaptive_k_sharded_matches_unsharded(group, name):
+    """Adaptive k under sharding: the blocks' (row shards') or the local batch's
+    row-variance sums are all-reduced before any row picks its k, so the
+    sharded forward selects as the unsharded one does."""
+    cfg = TEST_CONFIGS[name]
+    m = _model(cfg, adaptive=True)
+    x = make_input(cfg).cuda()
+    ref = m(x)
+    runner = ShardedGSA(m, group, T=cfg.T, B=cfg.B)
+    got = runner(runner.local_input(x))
+    if runner.mode == "batch":
+        assert torch.equal(got, ref)  # same GEMMs, same selection
+    err = (got.float() - ref.float()).abs().max().item()
+    rel = ((got.float() - ref.float()).norm() / ref.float().norm()).item()
+    assert err < 2e-2 and rel < 1e-2, (err, rel)
+    assert _lib.device_error() == 0
+

@@ -74,3 +74,47 @@ def test_gloo_world2_reassembles_row_and_batch_shards():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert all(ok_r and ok_b for _, ok_r, ok_b in res), res
+
+
+def _adaptive_worker(rank, world, port, T, q):
+    """Each rank holds its zig-zag rows' variances; ShardedGSA's all-reduce of
+    their sums must give every rank the batch-wide mean that adaptive k uses."""
+    from gsa_gdn_benchmarkstudy_b200.sharding import ShardedGSA
+    from oracle import gsa_oracle as O
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(11)
+        s = torch.randn(1, T, T, generator=g) * torch.linspace(0.5, 2.0, T).view(1, T, 1)
+        s = s.masked_fill(torch.triu(torch.ones(T, T, dtype=torch.bool), 1), float("-inf"))
+        var = O.score_variance(s)
+        runner = ShardedGSA(None, dist.group.WORLD, T=T, B=1)
+        mine = torch.cat([var[:, a:b] for a, b in runner.blocks], dim=1)
+        total = mine.double().sum().reshape(1)
+        runner._sum_over_ranks(total)
+        mean_ok = abs(total.item() / T - var.double().mean().item()) <= 1e-6 * var.mean().item()
+        ks = O.adaptive_k_from_variance(mine, 32, 4, 64, avg_var=(total / T).float().clamp(min=1e-6))
+        ref = O.adaptive_k_from_variance(var, 32, 4, 64)
+        ref_mine = torch.cat([ref[:, a:b] for a, b in runner.blocks], dim=1)
+        q.put((rank, mean_ok, int((ks != ref_mine).sum())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_world2_adaptive_k_variance_reduce():
+    world, T = 2, 64
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_adaptive_worker, args=(r, world, port, T, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in res), res
+    # k from the reduced mean matches the single-process rule (fp32 vs fp64
+    # means may move a row across a floor boundary; none does for this input)
+    assert all(bad == 0 for _, _, bad in res), res
