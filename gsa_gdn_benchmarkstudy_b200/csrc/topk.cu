@@ -48,6 +48,59 @@ __device__ __forceinline__ uint32_t ord_key(float f) {
 // ord_key(-inf) (0xFF800000 inverted): below every finite key.
 constexpr uint32_t kNegInfKey = 0x007FFFFFu;
 
+// Bin maps of the fast path.  Both give bin(f) = clamp((ord_key(f) - lo) >>
+// shift, 0, 2047) for finite f (-1 for -inf), monotonic in the key order, and
+// after set_threshold(b) classify f as gt (bin > b) / eq (bin == b).
+struct OrdBins {
+  uint32_t lo;
+  int shift;
+  int bstar = 0;
+  __device__ OrdBins(uint32_t lo_, int shift_) : lo(lo_), shift(shift_) {}
+  __device__ __forceinline__ int bin(float f) const {
+    const uint32_t u = ord_key(f);
+    if (u == kNegInfKey) return -1;
+    return u <= lo ? 0 : min(static_cast<int>((u - lo) >> shift), kBins - 1);
+  }
+  __device__ __forceinline__ void set_threshold(int b) { bstar = b; }
+  __device__ __forceinline__ void classify(float f, bool& gt, bool& eq) const {
+    const int bn = bin(f);
+    gt = bn > bstar;
+    eq = bn == bstar;
+  }
+};
+
+// The same map when lo is the key of a non-negative float, with raw = its
+// bits (lo - 0x80000000): non-negative floats' bits are already in key
+// order, every negative float (and -0.0) falls in bin 0 either way, so
+// bin(f) = clamp((max(bits, 0) - raw) >> shift, 0, 2047) as signed ints and
+// the gt / eq tests become two compares against the threshold bin's edges.
+struct PosBins {
+  int raw;
+  int shift;
+  int lo_edge = 0, hi_m1 = 0;
+  static constexpr int kNegInfBits = static_cast<int>(0xFF800000u);
+  __device__ PosBins(uint32_t raw_, int shift_) : raw(static_cast<int>(raw_)), shift(shift_) {}
+  __device__ __forceinline__ int bin(float f) const {
+    const int x = __float_as_int(f);
+    if (x == kNegInfBits) return -1;
+    const int d = max(max(x, 0) - raw, 0);
+    return min(d >> shift, kBins - 1);
+  }
+  // bin(f) > b  <=>  bits > hi_m1;  bin(f) >= b  <=>  bits >= lo_edge (b > 0).
+  // A key of bin b exists (b holds the k-th largest), so lo_edge fits in int.
+  __device__ __forceinline__ void set_threshold(int b) {
+    const long long lo64 = static_cast<long long>(raw) + (static_cast<long long>(b) << shift);
+    const long long hi64 = static_cast<long long>(raw) + (static_cast<long long>(b + 1) << shift) - 1;
+    lo_edge = b == 0 ? INT_MIN : static_cast<int>(min(lo64, static_cast<long long>(INT_MAX)));
+    hi_m1 = (b == kBins - 1 || hi64 > INT_MAX) ? INT_MAX : static_cast<int>(hi64);
+  }
+  __device__ __forceinline__ void classify(float f, bool& gt, bool& eq) const {
+    const int x = __float_as_int(f);
+    gt = x > hi_m1;
+    eq = !gt && x >= lo_edge && x != kNegInfBits;
+  }
+};
+
 struct TopkShared {
   int hist[kBins];
   uint32_t cand_key[kCandCap];
@@ -183,7 +236,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     uint32_t smin = 0xFFFFFFFFu, smax = 0u;
     int sfin = 0;
     {
-      const int p = static_cast<int>((static_cast<int64_t>(tid) * (n - 1)) / (kTopkThreads - 1));
+      // tid * (n - 1) < 2^31 here (n <= 32 * kMaxWords)
+      const int p = static_cast<int>(static_cast<uint32_t>(tid) * static_cast<uint32_t>(n - 1) /
+                                     static_cast<uint32_t>(kTopkThreads - 1));
       const uint32_t u = key_at(p);
       if (u != kNegInfKey) {
         smin = u;
@@ -201,135 +256,140 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
       const uint32_t lo = smin > margin ? smin - margin : 0u;
       const uint32_t span_w = min(0xFFFFFFFFu - lo, width + 2 * margin);
       const int shift = max(0, 32 - __clz(span_w) - kDigitBits);
-      auto bin_of = [&](uint32_t u) -> int {
-        return u <= lo ? 0 : min(static_cast<int>((u - lo) >> shift), kBins - 1);
-      };
-      // 2. histogram of finite keys
-      int nfin = 0;
-      auto hist_key = [&](float f) {
-        const uint32_t u = ord_key(f);
-        if (u != kNegInfKey) {
-          ++nfin;
-          atomicAdd(&sh.hist[bin_of(u)], 1);
-        }
-      };
-      int jv = 0;
-      if (vec_ok) {
-        const float4* s4 = reinterpret_cast<const float4*>(srow);
-        const int nv = n >> 2;
-        constexpr int U = 4;
-        for (int v0 = 0; v0 < nv; v0 += U * kTopkThreads) {
-          float4 f[U];
+      // Steps 2-5 for one bin map (OrdBins, or PosBins when the range starts
+      // at a non-negative float: the same bins from fewer integer ops).
+      // Returns false (block-uniformly) when the row needs the exact path.
+      auto fast = [&](auto bins) -> bool {
+        // 2. histogram of finite keys
+        auto hist_key = [&](float f) {
+          const int bn = bins.bin(f);
+          if (bn >= 0) atomicAdd(&sh.hist[bn], 1);
+        };
+        int jv = 0;
+        if (vec_ok) {
+          const float4* s4 = reinterpret_cast<const float4*>(srow);
+          const int nv = n >> 2;
+          constexpr int U = 4;
+          for (int v0 = 0; v0 < nv; v0 += U * kTopkThreads) {
+            float4 f[U];
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int v = v0 + u * kTopkThreads + tid;
-            f[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
+            for (int u = 0; u < U; ++u) {
+              const int v = v0 + u * kTopkThreads + tid;
+              f[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
-            if (v0 + u * kTopkThreads + tid < nv) {
-              hist_key(f[u].x);
-              hist_key(f[u].y);
-              hist_key(f[u].z);
-              hist_key(f[u].w);
+            for (int u = 0; u < U; ++u) {
+              if (v0 + u * kTopkThreads + tid < nv) {
+                hist_key(f[u].x);
+                hist_key(f[u].y);
+                hist_key(f[u].z);
+                hist_key(f[u].w);
+              }
             }
           }
+          jv = nv << 2;
         }
-        jv = nv << 2;
-      }
-      for (int j = jv + tid; j < n; j += kTopkThreads) hist_key(__ldg(srow + j));
-      uint32_t d0 = 0, d1 = 0;
-      block_minmax_count(sh, d0, d1, nfin);  // (syncs, so the histogram is complete)
-      if (nfin > k_sel) {
+        for (int j = jv + tid; j < n; j += kTopkThreads) hist_key(__ldg(srow + j));
+        __syncthreads();
+        // finite keys = histogram total
+        constexpr int kBpt = kBins / kTopkThreads;
+        int nfin = 0;
+#pragma unroll
+        for (int q = 0; q < kBpt; ++q) nfin += sh.hist[tid * kBpt + q];
+        uint32_t d0 = 0, d1 = 0;
+        block_minmax_count(sh, d0, d1, nfin);
+        if (nfin <= k_sel) return false;
         // 3. threshold bin
         find_threshold_bin(sh, k_sel);
         const int bstar = sh.sh_digit;
         const int krem = k_sel - sh.sh_above;
         const int bcount = sh.sh_bin;
-        if (bcount <= kCandCap) {
-          // 4. bits for higher bins, candidates of the threshold bin
-          const int seg = ((nwords + kTopkWarps - 1) / kTopkWarps) * 32;
-          const int s0 = min(warp * seg, nwords * 32), s1 = min(s0 + seg, nwords * 32);
-          // four 32-key groups per step: their loads are in flight together
-          constexpr int G = 4;
-          for (int jb = s0; jb < s1; jb += G * 32) {
-            uint32_t ug[G];
+        if (bcount > kCandCap) return false;
+        bins.set_threshold(bstar);
+        // 4. bits for higher bins, candidates of the threshold bin
+        const int seg = ((nwords + kTopkWarps - 1) / kTopkWarps) * 32;
+        const int s0 = min(warp * seg, nwords * 32), s1 = min(s0 + seg, nwords * 32);
+        // four 32-key groups per step: their loads are in flight together
+        constexpr int G = 4;
+        const float kNegInf = -__int_as_float(0x7F800000);
+        for (int jb = s0; jb < s1; jb += G * 32) {
+          float fg[G];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-              const int j = jb + g * 32 + lane;
-              ug[g] = (j < n && jb + g * 32 < s1) ? key_at(j) : kNegInfKey;
-            }
+          for (int g = 0; g < G; ++g) {
+            const int j = jb + g * 32 + lane;
+            fg[g] = (j < n && jb + g * 32 < s1) ? __ldg(srow + j) : kNegInf;
+          }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-              const int j0 = jb + g * 32;
-              if (j0 >= s1) break;
-              const int j = j0 + lane;
-              const uint32_t u = ug[g];
-              const int bn = u != kNegInfKey ? bin_of(u) : -1;
-              const uint32_t hib = __ballot_sync(0xFFFFFFFFu, bn > bstar);
-              if (bn == bstar) {
-                const int c = atomicAdd(&sh.n_cand, 1);
-                sh.cand_key[c] = u;
-                sh.cand_idx[c] = j;
-              }
-              if (lane == 0) sh.bits[j0 >> 5] = hib;
+          for (int g = 0; g < G; ++g) {
+            const int j0 = jb + g * 32;
+            if (j0 >= s1) break;
+            const int j = j0 + lane;
+            bool gt, eq;
+            bins.classify(fg[g], gt, eq);
+            const uint32_t hib = __ballot_sync(0xFFFFFFFFu, gt);
+            if (eq) {
+              const int c = atomicAdd(&sh.n_cand, 1);
+              sh.cand_key[c] = ord_key(fg[g]);
+              sh.cand_idx[c] = j;
             }
+            if (lane == 0) sh.bits[j0 >> 5] = hib;
           }
-          __syncthreads();
-          // 5. exact rank among the candidates: (key desc, index asc)
-          const int nc = sh.n_cand;
-          for (int c = tid; c < nc; c += kTopkThreads) {
-            const uint32_t u = sh.cand_key[c];
-            const int ji = sh.cand_idx[c];
-            int rank = 0;
-            for (int o = 0; o < nc; ++o) {
-              const uint32_t uo = sh.cand_key[o];
-              rank += (uo > u || (uo == u && sh.cand_idx[o] < ji)) ? 1 : 0;
-            }
-            if (rank < krem) atomicOr(&sh.bits[ji >> 5], 1u << (ji & 31));
-          }
-          __syncthreads();
-          if (brow) {
-            for (int64_t w = tid; w < bm_words; w += kTopkThreads)
-              brow[w] = w < nwords ? sh.bits[w] : 0u;
-          }
-          if (irow || mrow) {
-            // ascending column list from the bitmask; every pick is finite
-            const int wseg = (nwords + kTopkWarps - 1) / kTopkWarps;
-            const int w0 = min(warp * wseg, nwords), w1 = min(w0 + wseg, nwords);
-            int cnt = 0;
-            for (int w = w0 + lane; w < w1; w += 32) cnt += __popc(sh.bits[w]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
-            if (lane == 0) sh.warp_a[warp] = cnt;
-            __syncthreads();
-            int out = 0;
-            for (int w = 0; w < warp; ++w) out += sh.warp_a[w];
-            for (int wb = w0; wb < w1; wb += 32) {
-              const int w = wb + lane;
-              const uint32_t word = w < w1 ? sh.bits[w] : 0u;
-              const int pc = __popc(word);
-              int incl = pc;
-#pragma unroll
-              for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                if (lane >= o) incl += y;
-              }
-              int pos = out + incl - pc;
-              uint32_t rest = word;
-              while (rest) {
-                const int bit = __ffs(rest) - 1;
-                rest &= rest - 1;
-                if (irow) irow[pos] = w * 32 + bit;
-                if (mrow) mrow[pos] = 1;
-                ++pos;
-              }
-              out += __shfl_sync(0xFFFFFFFFu, incl, 31);
-            }
-          }
-          done = true;
         }
-      }
+        __syncthreads();
+        // 5. exact rank among the candidates: (key desc, index asc)
+        const int nc = sh.n_cand;
+        for (int c = tid; c < nc; c += kTopkThreads) {
+          const uint32_t u = sh.cand_key[c];
+          const int ji = sh.cand_idx[c];
+          int rank = 0;
+          for (int o = 0; o < nc; ++o) {
+            const uint32_t uo = sh.cand_key[o];
+            rank += (uo > u || (uo == u && sh.cand_idx[o] < ji)) ? 1 : 0;
+          }
+          if (rank < krem) atomicOr(&sh.bits[ji >> 5], 1u << (ji & 31));
+        }
+        __syncthreads();
+        if (brow) {
+          for (int64_t w = tid; w < bm_words; w += kTopkThreads)
+            brow[w] = w < nwords ? sh.bits[w] : 0u;
+        }
+        if (irow || mrow) {
+          // ascending column list from the bitmask; every pick is finite
+          const int wseg = (nwords + kTopkWarps - 1) / kTopkWarps;
+          const int w0 = min(warp * wseg, nwords), w1 = min(w0 + wseg, nwords);
+          int cnt = 0;
+          for (int w = w0 + lane; w < w1; w += 32) cnt += __popc(sh.bits[w]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+          if (lane == 0) sh.warp_a[warp] = cnt;
+          __syncthreads();
+          int out = 0;
+          for (int w = 0; w < warp; ++w) out += sh.warp_a[w];
+          for (int wb = w0; wb < w1; wb += 32) {
+            const int w = wb + lane;
+            const uint32_t word = w < w1 ? sh.bits[w] : 0u;
+            const int pc = __popc(word);
+            int incl = pc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+              if (lane >= o) incl += y;
+            }
+            int pos = out + incl - pc;
+            uint32_t rest = word;
+            while (rest) {
+              const int bit = __ffs(rest) - 1;
+              rest &= rest - 1;
+              if (irow) irow[pos] = w * 32 + bit;
+              if (mrow) mrow[pos] = 1;
+              ++pos;
+            }
+            out += __shfl_sync(0xFFFFFFFFu, incl, 31);
+          }
+        }
+        return true;
+      };
+      done = lo >= 0x80000000u ? fast(PosBins(lo - 0x80000000u, shift)) : fast(OrdBins(lo, shift));
     }
     __syncthreads();
   }
