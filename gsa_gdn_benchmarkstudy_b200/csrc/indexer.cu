@@ -6,12 +6,13 @@
 // Reference: GatedLightningIndexer.forward, gsa_ref.py:97-126 (fp32 math on
 // bf16-rounded projections; einsum, *scale, +bias, sigmoid, *sigmoid(w),
 // sum over heads in order h = 0..3, masked_fill(-inf)).  The tensor-core
-// epilogue evaluates the same terms two keys at a time with f32x2 FMAs:
-// y = dot*(-scale*log2 e) + (-bias*log2 e), sigmoid = 1/(1 + 2^y) with 2^y on
-// the MUFU and the reciprocal by Newton-Raphson on the FMA pipe (common.cuh,
-// sigmoid2_nr), acc += sigmoid * sigmoid(w) in head order; about 1e-7 from the
-// reference's separately rounded fp32 ops.  The fp32 CUDA-core kernel keeps
-// the reference's exact op order.
+// epilogue uses sigmoid(z) = 1/2 + tanh(z/2)/2: with hw_h = sigmoid(w_h)/2,
+// score = sum_h hw_h + sum_h hw_h * tanh(dot_h*scale/2 + bias_h/2), two keys
+// per f32x2 FMA and one MUFU tanh.approx per key and head (the cheapest
+// logistic on this SM: one MUFU op and two FMAs).  Scores come out about 1e-5
+// (relative) from the reference's separately rounded fp32 ops, inside the
+// 1e-2 bf16 budget.  The fp32 CUDA-core kernel keeps the reference's exact op
+// order.
 //
 // bf16 path: tcgen05 tensor cores.  One CTA owns 128 query rows and a chunk
 // of up to 512 keys.  Q (4 heads x [128 x 64] bf16) is loaded once by TMA
@@ -19,9 +20,11 @@
 // TMA ring.  Per sub-tile one thread issues 4 heads x 4 k-steps of
 // tcgen05.mma (M=128, N=32, K=16) into one of two TMEM accumulator buffers
 // (4 heads x 32 fp32 columns each; 256 columns per CTA so two CTAs share an
-// SM).  Four epilogue warps (thread = query row = TMEM lane) read the four
-// head accumulators with tcgen05.ld, apply the gated sum and the causal mask
-// and store fp32 scores.  Only key chunks at or below the diagonal run.
+// SM).  Eight epilogue warps, two per TMEM lane quarter (thread = query row =
+// TMEM lane), each read 16 of the 32 key columns of the four head
+// accumulators with tcgen05.ld, apply the gated sum and the causal mask and
+// store fp32 scores; at 94 registers, two 320-thread CTAs fit an SM.  Only
+// key chunks at or below the diagonal run.
 //
 // fp32 path: CUDA-core FFMA tiles (exact fp32 products, like the reference's
 // fp32 einsum), used for fp32 modules.
@@ -39,8 +42,10 @@ constexpr int kIdxD = 64;
 constexpr int kIdxQBytes = kIdxBM * kIdxD * 2;    // 16 KB per head
 constexpr int kIdxKBytes = kIdxBN * kIdxD * 2;    // 4 KB per stage
 constexpr int kIdxTmemCols = 256;                 // 2 buffers x 4 heads x 32
-constexpr int kIdxThreads = 192;                  // warps 0-3 epilogue, 4 TMA, 5 MMA
-constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kIdxEpiWarps = 8;                   // two per TMEM lane quarter, 16 columns each
+constexpr int kIdxTmaWarp = kIdxEpiWarps;         // warp 8: TMA producer
+constexpr int kIdxMmaWarp = kIdxEpiWarps + 1;     // warp 9: MMA issuer, TMEM owner
+constexpr int kIdxThreads = 32 * (kIdxEpiWarps + 2);
 constexpr long long kIdxDrainCycles = 200000000LL;  // ~0.1 s after an abort
 
 struct IdxSmem {
@@ -90,13 +95,13 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sh->acc_full[s], 1);
-      mbar_init(&sh->acc_empty[s], 4);
+      mbar_init(&sh->acc_empty[s], kIdxEpiWarps);
     }
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kIdxMmaWarp) {
     tmem_alloc(&sh->tmem_base, kIdxTmemCols);
     tmem_relinquish();
   }
@@ -106,7 +111,7 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
   const uint32_t tmem = sh->tmem_base;
   volatile int* abort = &sh->abort;
 
-  if (warp == 4) {
+  if (warp == kIdxTmaWarp) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tmap(&qmap);
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
           mbar_wait_drain(&sh->k_full[ss % kIdxStages], (ss / kIdxStages) & 1, kIdxDrainCycles);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kIdxMmaWarp) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(kIdxBM, kIdxBN, 0, 0);
@@ -160,12 +165,17 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ epilogue (warps 0-3)
-    const int i = tid;  // query row inside the tile == TMEM lane
+    // ------------------------------------------------ epilogue (warps 0-7)
+    // Warp w reads TMEM lanes 32*(w%4).. (its query rows) and the 16 key
+    // columns [16*(w/4), +16) of each 32-key sub-tile.
+    const int i = (warp & 3) * 32 + lane;  // query row inside the tile == TMEM lane
+    const int half = warp >> 2;
     const int r = row0 + i;
     const bool row_ok = r < a.Tq;
     const int pos = a.q_pos0 + r;
-    float sw[kIdxHeads], bh[kIdxHeads];
+    // sigmoid(z) = 1/2 + tanh(z/2)/2, so with hw_h = sigmoid(w_h)/2:
+    //   score = sum_h hw_h + sum_h hw_h * tanh(dot_h * scale/2 + bias_h/2)
+    float hw[kIdxHeads], hb[kIdxHeads], hsum = 0.f;
 #pragma unroll
     for (int h = 0; h < kIdxHeads; ++h) {
       float wv = 0.f;
@@ -174,37 +184,41 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
                                   (static_cast<int64_t>(b) * a.Tq + r) * a.w_stride + h;
         wv = __bfloat162float(*wp);
       }
-      sw[h] = sigmoid_ref(wv);
-      bh[h] = a.bias[h];
+      hw[h] = 0.5f * sigmoid_ref(wv);
+      hb[h] = 0.5f * a.bias[h];
+      hsum += hw[h];
     }
+    const float hscale = 0.5f * a.scale;
     float* orow = a.out + (static_cast<int64_t>(b) * a.Tq + r) * a.out_stride;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    constexpr int kCols = kIdxBN / 2;
     for (int s = 0; s < nsub; ++s) {
       const int buf = s & 1;
       if (!mbar_wait_warp(&sh->acc_full[buf], (s >> 1) & 1, a.err, abort)) break;
       tc_fence_after();
-      // score = sum_h sigmoid(w_h) * sigmoid(dot*scale + b_h), two keys per op:
-      // y = -(dot*scale + b_h)*log2(e), sigmoid = 1/(1 + 2^y)
-      uint64_t acc2[kIdxBN / 2];
+      // two keys per f32x2 op; tanh on the MUFU
+      uint64_t acc2[kCols / 2];
+#pragma unroll
+      for (int e = 0; e < kCols / 2; ++e) acc2[e] = f2_pack(hsum, hsum);
 #pragma unroll
       for (int h = 0; h < kIdxHeads; ++h) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + buf * 128 + h * kIdxBN, raw);
+        uint32_t raw[kCols];
+        tmem_ld16(tmem + lane_base + buf * 128 + h * kIdxBN + half * kCols, raw);
         tc_wait_ld();
-        const uint64_t ys = f2_pack(-a.scale * kLog2e, -a.scale * kLog2e);
-        const uint64_t yb = f2_pack(-bh[h] * kLog2e, -bh[h] * kLog2e);
-        const uint64_t w2 = f2_pack(sw[h], sw[h]);
+        const uint64_t zs = f2_pack(hscale, hscale);
+        const uint64_t zb = f2_pack(hb[h], hb[h]);
+        const uint64_t w2 = f2_pack(hw[h], hw[h]);
 #pragma unroll
-        for (int e = 0; e < kIdxBN; e += 2) {
-          const uint64_t y2 =
-              f2_fma(f2_pack(__uint_as_float(raw[e]), __uint_as_float(raw[e + 1])), ys, yb);
-          const uint64_t g2 = sigmoid2_nr(y2);
-          acc2[e >> 1] = h == 0 ? f2_fma(g2, w2, 0ull) : f2_fma(g2, w2, acc2[e >> 1]);
+        for (int e = 0; e < kCols; e += 2) {
+          const uint64_t z2 =
+              f2_fma(f2_pack(__uint_as_float(raw[e]), __uint_as_float(raw[e + 1])), zs, zb);
+          const uint64_t t2 = f2_pack(fast_tanh(f2_lo(z2)), fast_tanh(f2_hi(z2)));
+          acc2[e >> 1] = f2_fma(t2, w2, acc2[e >> 1]);
         }
       }
-      float acc[kIdxBN];
+      float acc[kCols];
 #pragma unroll
-      for (int e = 0; e < kIdxBN; e += 2) {
+      for (int e = 0; e < kCols; e += 2) {
         acc[e] = f2_lo(acc2[e >> 1]);
         acc[e + 1] = f2_hi(acc2[e >> 1]);
       }
@@ -212,18 +226,18 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->acc_empty[buf]);
       if (row_ok) {
-        const int j0 = key0 + s * kIdxBN;
+        const int j0 = key0 + s * kIdxBN + half * kCols;
 #pragma unroll
-        for (int e = 0; e < kIdxBN; ++e)
+        for (int e = 0; e < kCols; ++e)
           if (j0 + e > pos) acc[e] = -INFINITY;
-        if (j0 + kIdxBN <= a.Tkv) {
+        if (j0 + kCols <= a.Tkv) {
           float4* dst = reinterpret_cast<float4*>(orow + j0);
 #pragma unroll
-          for (int v = 0; v < kIdxBN / 4; ++v)
+          for (int v = 0; v < kCols / 4; ++v)
             dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
         } else {
 #pragma unroll
-          for (int e = 0; e < kIdxBN; ++e)
+          for (int e = 0; e < kCols; ++e)
             if (j0 + e < a.Tkv) orow[j0 + e] = acc[e];
         }
       }
@@ -232,7 +246,7 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kIdxMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kIdxTmemCols);
   }

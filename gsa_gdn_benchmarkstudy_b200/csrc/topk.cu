@@ -6,13 +6,15 @@
 // ascending index sort of gsa_opt.py:674-677.  Ties are broken toward the
 // lower key index (torch.topk leaves tie order unspecified).
 //
-// One CTA of 256 threads per query row; the row has n = min(q_pos0 + r + 1,
+// One CTA of 128 threads per query row; the row has n = min(q_pos0 + r + 1,
 // Tkv) keys.  Scores become order-preserving uint32 keys (ord_key).
 //
 // Fast path (rows with n > k, the common case):
-//  1. 256 keys sampled evenly over the row give a key range [lo, hi], widened
-//     by a quarter on each side; bin(u) = clamp((u - lo) >> shift, 0, 2047)
-//     is monotonic in u.
+//  1. One key per thread, sampled evenly over the row, gives a key range
+//     [lo, hi], widened by a quarter on each side; bin(u) = clamp((u - lo) >>
+//     shift, 0, 2047) is monotonic in u.  When lo is the key of a
+//     non-negative float (indexer scores always are), the same bins come from
+//     the raw float bits with fewer integer ops (PosBins).
 //  2. One read of the row builds the 2048-bin histogram of finite keys.
 //  3. The bin holding the k-th largest key is found by a suffix scan.
 //  4. A second read emits, per 32 keys, a ballot of the keys in higher bins
@@ -31,7 +33,12 @@
 namespace gsa {
 namespace {
 
-constexpr int kTopkThreads = 256;
+#ifndef GSA_TOPK_THREADS
+#define GSA_TOPK_THREADS 128
+#endif
+constexpr int kTopkThreads = GSA_TOPK_THREADS;  // threads per row (a power of two, 128..1024)
+static_assert(kTopkThreads >= 128 && kTopkThreads <= 1024 && (kTopkThreads & (kTopkThreads - 1)) == 0,
+              "threads per row");
 constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kBins = 2048;   // 11-bit digits / histogram bins
 constexpr int kDigitBits = 11;
@@ -61,6 +68,12 @@ struct OrdBins {
     if (u == kNegInfKey) return -1;
     return u <= lo ? 0 : min(static_cast<int>((u - lo) >> shift), kBins - 1);
   }
+  // histogram slot of f and 1 if f counts (finite), without a branch
+  __device__ __forceinline__ int hist_bin(float f, int& inc) const {
+    const uint32_t u = ord_key(f);
+    inc = u != kNegInfKey ? 1 : 0;
+    return u <= lo ? 0 : min(static_cast<int>((u - lo) >> shift), kBins - 1);
+  }
   __device__ __forceinline__ void set_threshold(int b) { bstar = b; }
   __device__ __forceinline__ void classify(float f, bool& gt, bool& eq) const {
     const int bn = bin(f);
@@ -80,11 +93,11 @@ struct PosBins {
   int lo_edge = 0, hi_m1 = 0;
   static constexpr int kNegInfBits = static_cast<int>(0xFF800000u);
   __device__ PosBins(uint32_t raw_, int shift_) : raw(static_cast<int>(raw_)), shift(shift_) {}
-  __device__ __forceinline__ int bin(float f) const {
+  // -inf is a negative float: bin 0, not counted
+  __device__ __forceinline__ int hist_bin(float f, int& inc) const {
     const int x = __float_as_int(f);
-    if (x == kNegInfBits) return -1;
-    const int d = max(max(x, 0) - raw, 0);
-    return min(d >> shift, kBins - 1);
+    inc = x != kNegInfBits ? 1 : 0;
+    return min(max(max(x, 0) - raw, 0) >> shift, kBins - 1);
   }
   // bin(f) > b  <=>  bits > hi_m1;  bin(f) >= b  <=>  bits >= lo_edge (b > 0).
   // A key of bin b exists (b holds the k-th largest), so lo_edge fits in int.
@@ -262,8 +275,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
       auto fast = [&](auto bins) -> bool {
         // 2. histogram of finite keys
         auto hist_key = [&](float f) {
-          const int bn = bins.bin(f);
-          if (bn >= 0) atomicAdd(&sh.hist[bn], 1);
+          int inc;
+          const int bn = bins.hist_bin(f, inc);
+          atomicAdd(&sh.hist[bn], inc);
         };
         int jv = 0;
         if (vec_ok) {
@@ -312,28 +326,34 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
         // four 32-key groups per step: their loads are in flight together
         constexpr int G = 4;
         const float kNegInf = -__int_as_float(0x7F800000);
-        for (int jb = s0; jb < s1; jb += G * 32) {
+        auto emit_group = [&](int j0, float f) {
+          bool gt, eq;
+          bins.classify(f, gt, eq);
+          const uint32_t hib = __ballot_sync(0xFFFFFFFFu, gt);
+          const uint32_t eqb = __ballot_sync(0xFFFFFFFFu, eq);
+          if (eqb) {  // warp-uniform; one atomic per warp
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&sh.n_cand, __popc(eqb));
+            base = __shfl_sync(0xFFFFFFFFu, base, 0);
+            if (eq) {
+              const int c = base + __popc(eqb & lt_mask);
+              sh.cand_key[c] = ord_key(f);
+              sh.cand_idx[c] = j0 + lane;
+            }
+          }
+          if (lane == 0) sh.bits[j0 >> 5] = hib;
+        };
+        const int full_end = s0 + max(0, min(s1, n) - s0) / (G * 32) * (G * 32);
+        for (int jb = s0; jb < full_end; jb += G * 32) {  // whole steps inside the row
           float fg[G];
 #pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const int j = jb + g * 32 + lane;
-            fg[g] = (j < n && jb + g * 32 < s1) ? __ldg(srow + j) : kNegInf;
-          }
+          for (int g = 0; g < G; ++g) fg[g] = __ldg(srow + jb + g * 32 + lane);
 #pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const int j0 = jb + g * 32;
-            if (j0 >= s1) break;
-            const int j = j0 + lane;
-            bool gt, eq;
-            bins.classify(fg[g], gt, eq);
-            const uint32_t hib = __ballot_sync(0xFFFFFFFFu, gt);
-            if (eq) {
-              const int c = atomicAdd(&sh.n_cand, 1);
-              sh.cand_key[c] = ord_key(fg[g]);
-              sh.cand_idx[c] = j;
-            }
-            if (lane == 0) sh.bits[j0 >> 5] = hib;
-          }
+          for (int g = 0; g < G; ++g) emit_group(jb + g * 32, fg[g]);
+        }
+        for (int j0 = full_end; j0 < s1; j0 += 32) {  // ragged tail, checked
+          const int j = j0 + lane;
+          emit_group(j0, j < n ? __ldg(srow + j) : kNegInf);
         }
         __syncthreads();
         // 5. exact rank among the candidates: (key desc, index asc)
