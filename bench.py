@@ -299,6 +299,11 @@ def run_ours(args, cfg, rank: int, world: int, device):
     out_host = torch.empty(cfg.B, cfg.T, cfg.D, dtype=cfg.torch_dtype).pin_memory()
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
+    for _ in range(args.warmup):  # untimed, as for the device-resident steps
+        if e2e_step is None:
+            model.forward_host(x_host, out=out_host)
+        else:
+            e2e_step()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

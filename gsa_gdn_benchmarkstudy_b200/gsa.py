@@ -321,18 +321,21 @@ class GatedSparseAttention(nn.Module):
         }
 
     def select_rows(self, parts: dict, ik_all: torch.Tensor, q_pos0: int,
-                    tkv: Optional[int] = None):
+                    tkv: Optional[int] = None, bitmask_out: Optional[torch.Tensor] = None):
         """Indexer + top-k for a block of query rows (``parts`` = the block's projection views).
 
         Returns the selection: a bitmask [B, Tq, W] for the tensor-core attention
-        (bf16, d_head = 128), else (indices, mask) for the index-gather path."""
+        (bf16, d_head = 128; written into ``bitmask_out`` when given, else into
+        scratch kept per stream), else (indices, mask) for the index-gather path."""
         Tkv = ik_all.shape[1] if tkv is None else tkv
         bf16_tc = parts["iq"].dtype == torch.bfloat16 and self.d_head == 128
         B, Tq = parts["iq"].shape[:2]
         sel = self.topk_selector
         if sel.adaptive:
             need = ops.indexer_topk_adaptive_workspace_size(B, Tq, Tkv)
-            ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc, need)
+            ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc and bitmask_out is None,
+                                   need)
+            bm = bitmask_out if bitmask_out is not None else bm
             with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=4):
                 idx, mask, bitmask, _ = ops.indexer_topk_adaptive(
                     parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale,
@@ -341,8 +344,9 @@ class GatedSparseAttention(nn.Module):
                     workspace=ws, bitmask_out=bm)
             return bitmask if bf16_tc else (idx, mask)
         k_eff = sel.k_effective(Tkv)
-        ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc,
+        ws, bm = self._scratch(parts["iq"].device, B, Tq, Tkv, bf16_tc and bitmask_out is None,
                                ops.indexer_topk_workspace_size(B, Tq, Tkv))
+        bm = bitmask_out if bitmask_out is not None else bm
         with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
             idx, mask, bitmask = ops.indexer_topk(
                 parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
@@ -555,7 +559,14 @@ class GatedSparseAttention(nn.Module):
         return pair
 
     def _forward_host_rows(self, x_host, out, chunks, dev, compute, h2d, d2h):
-        """B == 1: row blocks [r0, r1) in sequence order, keys [0, r1) for each."""
+        """B == 1: row blocks [r0, r1) in sequence order, keys [0, r1) for each.
+
+        Two compute streams: the side stream prepares block c (projection GEMM,
+        indexer + top-k into block c's rows of a whole-sequence bitmask, RoPE +
+        value gate) as soon as its input has arrived, and the current stream
+        runs block c's attention and o_proj once block c is prepared.  The
+        preparation of block c+1 therefore fills the SMs that the tail of
+        block c's attention leaves idle."""
         _, T, D = x_host.shape
         H = self.num_heads
         tiles = (T + 127) // 128
@@ -576,6 +587,12 @@ class GatedSparseAttention(nn.Module):
         v = torch.empty_like(q)
         attn = torch.empty_like(q)
         y = torch.empty_like(q)
+        bf16_tc = x_host.dtype == torch.bfloat16 and self.d_head == 128
+        # one contiguous [1, r1 - r0, bitmask_words(r1)] selection per block, all alive at once
+        bm_sizes = [(r1 - r0) * ops.bitmask_words(r1) for r0, r1 in zip(bounds[:-1], bounds[1:])]
+        bm_flat = (torch.empty(sum(bm_sizes), device=dev, dtype=torch.int32) if bf16_tc
+                   else None)
+        bm_offs = [sum(bm_sizes[:i]) for i in range(len(bm_sizes))]
         done_in = []
         for r0, r1 in zip(bounds[:-1], bounds[1:]):
             with torch.cuda.stream(h2d):
@@ -585,20 +602,36 @@ class GatedSparseAttention(nn.Module):
                 done_in.append(e)
         parts_all = self.split(proj)
         side = self._side_stream(dev)
-        for c, (r0, r1) in enumerate(zip(bounds[:-1], bounds[1:])):
-            compute.wait_event(done_in[c])
-            with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
-                torch.addmm(bias, x_dev[0, r0:r1], w.t(), out=proj[0, r0:r1])
-            rows = {name: t[:, r0:r1] for name, t in parts_all.items()}
-            # indexer + top-k on the side stream beside RoPE + value gate, as in forward
-            side.wait_stream(compute)
+        side.wait_stream(compute)  # the buffers above come from the current stream's pool
+        blocks = list(zip(bounds[:-1], bounds[1:]))
+
+        def prepare(c):
+            r0, r1 = blocks[c]
             with torch.cuda.stream(side):
-                sel = self.select_rows(rows, parts_all["ik"][:, :r1], q_pos0=r0, tkv=r1)
-            with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
-                ops.rope_gates(rows["q"], rows["k"], cos[r0:r1], sin[r0:r1], H,
-                               v_src=rows["v"], vg_src=rows["vg"],
-                               out=(q[:, r0:r1], k[:, r0:r1], v[:, r0:r1]))
-            compute.wait_stream(side)
+                side.wait_event(done_in[c])
+                with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
+                    torch.addmm(bias, x_dev[0, r0:r1], w.t(), out=proj[0, r0:r1])
+                rows = {name: t[:, r0:r1] for name, t in parts_all.items()}
+                bm_c = (bm_flat[bm_offs[c]:bm_offs[c] + bm_sizes[c]].view(
+                    1, r1 - r0, ops.bitmask_words(r1)) if bf16_tc else None)
+                sel = self.select_rows(rows, parts_all["ik"][:, :r1], q_pos0=r0, tkv=r1,
+                                       bitmask_out=bm_c)
+                with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
+                    ops.rope_gates(rows["q"], rows["k"], cos[r0:r1], sin[r0:r1], H,
+                                   v_src=rows["v"], vg_src=rows["vg"],
+                                   out=(q[:, r0:r1], k[:, r0:r1], v[:, r0:r1]))
+                e = torch.cuda.Event()
+                e.record(side)
+            return e, rows, sel
+
+        # issue order: the preparation of block c+1 is queued before the attention
+        # of block c, so neither stream waits on the host
+        prepared = [prepare(0)]
+        for c, (r0, r1) in enumerate(blocks):
+            if c + 1 < len(blocks):
+                prepared.append(prepare(c + 1))
+            e, rows, sel = prepared[c]
+            compute.wait_event(e)
             if isinstance(sel, tuple):
                 for t in sel:
                     t.record_stream(compute)
@@ -614,6 +647,7 @@ class GatedSparseAttention(nn.Module):
             d2h.wait_stream(compute)
             with torch.cuda.stream(d2h):
                 out[:, r0:r1].copy_(y[:, r0:r1], non_blocking=True)
+        compute.wait_stream(side)
         y.record_stream(d2h)
         compute.wait_stream(d2h)
         d2h.synchronize()
