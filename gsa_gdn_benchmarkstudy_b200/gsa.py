@@ -106,11 +106,19 @@ class RotaryEmbedding(nn.Module):
             self._set_cos_sin_cache(seq_len)
             self.cos_cached = self.cos_cached.to(device)
             self.sin_cached = self.sin_cached.to(device)
+        # the converted tables are kept until the cache tensors change (rebuild,
+        # .to(), in-place edits), so a steady forward launches no conversion kernels
+        key = (seq_len, torch.device(device), dtype, self.cos_cached.data_ptr(),
+               self.cos_cached._version, self.sin_cached.data_ptr(), self.sin_cached._version)
+        hit = getattr(self, "_tables", None)
+        if hit is not None and hit[0] == key:
+            return hit[1], hit[2]
         cos = self.cos_cached[:seq_len].to(device)
         sin = self.sin_cached[:seq_len].to(device)
         if dtype is not None:
             cos = cos.to(dtype)
             sin = sin.to(dtype)
+        self._tables = (key, cos, sin)
         return cos, sin
 
 
@@ -142,6 +150,17 @@ class GatedLightningIndexer(nn.Module):
         nn.init.xavier_uniform_(self.idx_q_proj.weight, gain=1.0)
         nn.init.xavier_uniform_(self.idx_k_proj.weight, gain=1.0)
         nn.init.xavier_uniform_(self.idx_w_proj.weight, gain=0.1)
+
+    def bias_f32(self) -> torch.Tensor:
+        """idx_bias as contiguous float32 (what the kernels read), converted once
+        per change of the parameter rather than on every call."""
+        p = self.idx_bias
+        key = (p.data_ptr(), p._version, p.device, p.dtype)
+        hit = getattr(self, "_bias32", None)
+        if hit is None or hit[0] != key:
+            hit = (key, p.detach().to(torch.float32).contiguous())
+            self._bias32 = hit
+        return hit[1]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, _ = x.shape
@@ -338,7 +357,7 @@ class GatedSparseAttention(nn.Module):
             bm = bitmask_out if bitmask_out is not None else bm
             with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=4):
                 idx, mask, bitmask, _ = ops.indexer_topk_adaptive(
-                    parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale,
+                    parts["iq"], ik_all, parts["iw"], self.indexer.bias_f32(), self.indexer.scale,
                     sel.k_base, sel.k_min, sel.k_max, q_pos0=q_pos0, tkv=Tkv,
                     want_indices=not bf16_tc, want_mask=not bf16_tc, want_bitmask=bf16_tc,
                     workspace=ws, bitmask_out=bm)
@@ -349,7 +368,7 @@ class GatedSparseAttention(nn.Module):
         bm = bitmask_out if bitmask_out is not None else bm
         with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=2):
             idx, mask, bitmask = ops.indexer_topk(
-                parts["iq"], ik_all, parts["iw"], self.indexer.idx_bias, self.indexer.scale, k_eff,
+                parts["iq"], ik_all, parts["iw"], self.indexer.bias_f32(), self.indexer.scale, k_eff,
                 q_pos0=q_pos0, tkv=Tkv, want_indices=not bf16_tc, want_mask=not bf16_tc,
                 want_bitmask=bf16_tc, workspace=ws, bitmask_out=bm)
         return bitmask if bf16_tc else (idx, mask)
@@ -375,7 +394,7 @@ class GatedSparseAttention(nn.Module):
             ws, bm = self._scratch(p["iq"].device, B, Tq, tkv, bf16_tc, need, slot=slot)
             scores, row_var, var_sum = ops.adaptive_workspace_views(ws, B, Tq, tkv)
             with _Stage(self, "k:indexer_topk", "gsa_b200/indexer_topk", launches=3):
-                ops.indexer_scores(p["iq"], ik, p["iw"], self.indexer.idx_bias,
+                ops.indexer_scores(p["iq"], ik, p["iw"], self.indexer.bias_f32(),
                                    self.indexer.scale, q_pos0=q0, tkv=tkv, fill_upper=False,
                                    out=scores)
                 ops.row_variance(scores[:, :, :tkv], q_pos0=q0, out=(row_var, var_sum))
