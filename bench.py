@@ -396,6 +396,8 @@ def time_indexer_and_topk(model, x, cfg, iters: int = 5):
     res = {}
     scores = ops.indexer_scores(parts["iq"], parts["ik"], parts["iw"], ix.idx_bias, ix.scale,
                                 fill_upper=False)
+    # one bitmask for every call: allocations do not land between the timing events
+    bm = torch.empty(cfg.B, cfg.T, ops.bitmask_words(cfg.T), device=x.device, dtype=torch.int32)
     for name in ("indexer", "topk"):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -406,7 +408,8 @@ def time_indexer_and_topk(model, x, cfg, iters: int = 5):
                                        (cfg.B, cfg.T, scores.stride(1)),
                                        (scores.stride(0), scores.stride(1), 1)))
             else:
-                ops.topk_select(scores, k_eff, want_indices=False, want_mask=False)
+                ops.topk_select(scores, k_eff, want_indices=False, want_mask=False,
+                                bitmask_out=bm)
         e1.record()
         torch.cuda.synchronize()
         res[name] = e0.elapsed_time(e1) / iters

@@ -344,14 +344,15 @@ def topk_select_adaptive(scores: torch.Tensor, k_base: int, k_min: int, k_max: i
 
 # --------------------------------------------------------------------------- top-k
 def topk_select(scores: torch.Tensor, k_sel: int, q_pos0: int = 0, want_indices: bool = True,
-                want_mask: bool = True, want_bitmask: bool = True):
+                want_mask: bool = True, want_bitmask: bool = True,
+                bitmask_out: torch.Tensor | None = None):
     """Top-k over causal rows of ``scores`` [B, Tq, Tkv] (fp32, unit inner stride).
 
     Returns (indices int32 [B,Tq,k] ascending + masked filler, mask bool [B,Tq,k],
     bitmask int32-storage uint32 words [B,Tq,W]); unrequested outputs are None."""
     B, Tq, Tkv = _check_scores(scores)
     idx, msk, bm, W = _selection_outputs(scores.device, B, Tq, k_sel, Tkv, want_indices,
-                                         want_mask, want_bitmask)
+                                         want_mask, want_bitmask, bitmask_out)
     rc = _lib.load().gsa_topk_select(
         scores.data_ptr(), scores.stride(1), B, Tq, Tkv, int(q_pos0), int(k_sel),
         _ptr(idx), _ptr(msk), _ptr(bm), W, _stream())
