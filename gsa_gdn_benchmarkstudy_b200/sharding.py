@@ -62,17 +62,30 @@ def all_gather_equal(t: torch.Tensor, group) -> torch.Tensor:
     return out
 
 
-def gather_rows(local: torch.Tensor, T: int, group) -> torch.Tensor:
-    """Reassemble zig-zag row shards [1, Tl, W] from every rank into [1, T, W] in sequence order."""
-    world = dist.get_world_size(group)
-    g = all_gather_equal(local[0], group)  # [world, Tl, W]
-    full = torch.empty((1, T, local.shape[-1]), dtype=local.dtype, device=local.device)
+def zigzag_order(T: int, world: int, device) -> torch.Tensor:
+    """For each sequence row, its row in the rank-major all-gather of zig-zag shards."""
+    src = torch.empty(T, dtype=torch.long)
+    tl = T // world
     for r in range(world):
         off = 0
         for s, e in zigzag_blocks(T, world, r):
-            full[0, s:e] = g[r, off:off + (e - s)]
+            src[s:e] = torch.arange(r * tl + off, r * tl + off + (e - s))
             off += e - s
-    return full
+    return src.to(device)
+
+
+def unshard_rows(g: torch.Tensor, order: torch.Tensor) -> torch.Tensor:
+    """[world, Tl, W] gathered shards -> [1, T, W] in sequence order (one gather kernel)."""
+    return g.reshape(-1, g.shape[-1]).index_select(0, order).unsqueeze(0)
+
+
+def gather_rows(local: torch.Tensor, T: int, group, order: torch.Tensor = None) -> torch.Tensor:
+    """Reassemble zig-zag row shards [1, Tl, W] from every rank into [1, T, W] in sequence order."""
+    world = dist.get_world_size(group)
+    g = all_gather_equal(local[0], group)  # [world, Tl, W]
+    if order is None:
+        order = zigzag_order(T, world, local.device)
+    return unshard_rows(g, order)
 
 
 def gather_batch(local: torch.Tensor, group) -> torch.Tensor:
@@ -105,13 +118,38 @@ class ShardedGSA:
             per = B // self.world
             self.b0, self.b1 = self.rank * per, (self.rank + 1) * per
         self._pos = None
+        self._order = None
         self._host_out = None
+        self._bitmasks = None
+        # K/V all-gathers run on a high-priority NCCL stream of their own group, beside
+        # the indexer + top-k (new_group is collective: every rank builds it here)
+        self.kv_group = group
+        if self.mode == "rows" and dist.get_backend(group) == "nccl":
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+            self.kv_group = dist.new_group(ranks=dist.get_process_group_ranks(group),
+                                           backend="nccl", pg_options=opts)
 
     # ---------------------------------------------------------------- inputs
     def local_input(self, x: torch.Tensor) -> torch.Tensor:
         if self.mode == "rows":
             return torch.cat([x[:, s:e] for s, e in self.blocks], dim=1).contiguous()
         return x[self.b0:self.b1].contiguous()
+
+    def _row_order(self, device) -> torch.Tensor:
+        if self._order is None or self._order.device != device:
+            self._order = zigzag_order(self.T, self.world, device)
+        return self._order
+
+    def _block_bitmasks(self, device):
+        """One selection bitmask per row block, alive together (both blocks select
+        before either attends)."""
+        key = (device, tuple(self.blocks))
+        if self._bitmasks is None or self._bitmasks[0] != key:
+            bms = [torch.empty(1, e - s, ops.bitmask_words(e), device=device, dtype=torch.int32)
+                   for s, e in self.blocks]
+            self._bitmasks = (key, bms)
+        return self._bitmasks[1]
 
     def _positions(self, device) -> torch.Tensor:
         if self._pos is None or self._pos.device != device:
@@ -142,18 +180,29 @@ class ShardedGSA:
     def _forward_rows(self, x_loc: torch.Tensor, gather: bool = True) -> torch.Tensor:
         m = self.model
         T, D, H = self.T, m.hidden_size, m.num_heads
+        dev = x_loc.device
+        order = self._row_order(dev)
         proj = m.project(x_loc)
         parts = m.split(proj)
-        cos, sin = m.rotary_emb(T, x_loc.device, x_loc.dtype)
-        pos = self._positions(x_loc.device)
+        # the selection needs only the indexer keys of the whole sequence (2 MB at T=16K)
+        ik_full = gather_rows(parts["ik"].contiguous(), T, self.group, order)
+        cos, sin = m.rotary_emb(T, dev, x_loc.dtype)
+        pos = self._positions(dev)
         q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
                                  sin.index_select(0, pos), H, v_src=parts["v"],
                                  vg_src=parts["vg"])
-        # keys, values and indexer keys of the whole sequence on every rank
-        k_full = gather_rows(k, T, self.group)
-        v_full = gather_rows(v, T, self.group)
-        ik_full = gather_rows(parts["ik"].contiguous(), T, self.group)
-        outs, blocks, off = [], [], 0
+        # keys and values of the whole sequence: gathered while the blocks select
+        gk = torch.empty((self.world, *k.shape[1:]), dtype=k.dtype, device=dev)
+        gv = torch.empty_like(gk)
+        if dist.get_backend(self.kv_group) == "nccl":
+            wk = dist.all_gather_into_tensor(gk, k[0], group=self.kv_group, async_op=True)
+            wv = dist.all_gather_into_tensor(gv, v[0], group=self.kv_group, async_op=True)
+        else:
+            wk = dist.all_gather(list(gk.unbind(0)), k[0].contiguous(), group=self.kv_group,
+                                 async_op=True)
+            wv = dist.all_gather(list(gv.unbind(0)), v[0].contiguous(), group=self.kv_group,
+                                 async_op=True)
+        blocks, off = [], 0
         for s, e in self.blocks:
             n = e - s
             pb = {key: parts[key][:, off:off + n] for key in ("iq", "iw", "og")}
@@ -163,16 +212,19 @@ class ShardedGSA:
             # every row's k needs the mean row variance over all ranks' rows
             sels = m.select_blocks([(pb, ik_full[:, :e], s, e) for pb, s, e, _, _ in blocks],
                                    var_reduce=self._sum_over_ranks, var_rows=self.B * T)
-            for (pb, s, e, o, n), sel in zip(blocks, sels):
-                outs.append(m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e],
-                                              q[:, o:o + n], q_pos0=s))
         else:
-            for pb, s, e, o, n in blocks:
-                outs.append(m.attend_rows(pb, k_full[:, :e], v_full[:, :e], ik_full[:, :e],
-                                          q[:, o:o + n], q_pos0=s))
+            bms = self._block_bitmasks(dev)
+            sels = [m.select_rows(pb, ik_full[:, :e], s, tkv=e, bitmask_out=bm)
+                    for (pb, s, e, _, _), bm in zip(blocks, bms)]
+        wk.wait()
+        wv.wait()
+        k_full = unshard_rows(gk, order)
+        v_full = unshard_rows(gv, order)
+        outs = [m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e], q[:, o:o + n], q_pos0=s)
+                for (pb, s, e, o, n), sel in zip(blocks, sels)]
         attn = torch.cat(outs, dim=1)
         out_local = F.linear(attn, m.o_proj.weight)
-        return gather_rows(out_local, T, self.group) if gather else out_local
+        return gather_rows(out_local, T, self.group, order) if gather else out_local
 
     def forward_host(self, x_local_host: torch.Tensor) -> torch.Tensor:
         """This rank's input share from pinned host memory -> device, sharded forward,
