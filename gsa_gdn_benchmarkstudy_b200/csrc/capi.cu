@@ -207,8 +207,10 @@ int indexer_topk_impl(const void* q, int64_t q_stride, const void* k, int64_t k_
   int rc = indexer_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
                         q_pos0, H_I, d_I, scores, stride, 0, s);
   if (rc) return rc;
+  // the indexer writes finite scores into every valid column
   return finish(gsa::launch_topk(scores, stride, B, Tq, Tkv, q_pos0, k_sel, k_sel,
-                                 gsa::AdaptiveK{}, indices, mask, bitmask, bitmask_words, s));
+                                 gsa::AdaptiveK{}, indices, mask, bitmask, bitmask_words,
+                                 /*finite_rows=*/true, s));
 }
 
 // Adaptive-k workspace: the score rows, then row_var [B*Tq] floats, then the
@@ -371,7 +373,7 @@ int gsa_topk_select(const float* scores, int64_t score_stride, int B, int Tq, in
   if (rc) return rc;
   return finish(gsa::launch_topk(scores, score_stride, B, Tq, Tkv, q_pos0, k_sel, k_sel,
                                  gsa::AdaptiveK{}, indices, mask, bitmask, bitmask_words,
-                                 static_cast<cudaStream_t>(stream)));
+                                 /*finite_rows=*/false, static_cast<cudaStream_t>(stream)));
 }
 
 int gsa_row_variance(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
@@ -391,11 +393,12 @@ int gsa_row_variance(const float* scores, int64_t score_stride, int B, int Tq, i
                                          var_sum, s));
 }
 
-int gsa_topk_select_adaptive(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
-                             int q_pos0, int k_base, int k_min, int k_max, const float* row_var,
-                             const double* var_sum, int64_t var_rows, int32_t* row_k,
-                             int32_t* indices, uint8_t* mask, uint32_t* bitmask,
-                             int64_t bitmask_words, void* stream) {
+namespace {
+int topk_select_adaptive_impl(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                              int q_pos0, int k_base, int k_min, int k_max, const float* row_var,
+                              const double* var_sum, int64_t var_rows, int32_t* row_k,
+                              int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                              int64_t bitmask_words, bool finite_rows, void* stream) {
   if (B < 0 || Tq < 0 || Tkv <= 0 || q_pos0 < 0) return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
   int rc = check_adaptive_k(k_base, k_min, k_max);
   if (rc) return rc;
@@ -419,7 +422,19 @@ int gsa_topk_select_adaptive(const float* scores, int64_t score_stride, int B, i
   ad.row_k = row_k;
   const int width = gsa_adaptive_k_width(k_max, Tkv);
   return finish(gsa::launch_topk(scores, score_stride, B, Tq, Tkv, q_pos0, 0, width, ad, indices,
-                                 mask, bitmask, bitmask_words, static_cast<cudaStream_t>(stream)));
+                                 mask, bitmask, bitmask_words, finite_rows,
+                                 static_cast<cudaStream_t>(stream)));
+}
+}  // namespace
+
+int gsa_topk_select_adaptive(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
+                             int q_pos0, int k_base, int k_min, int k_max, const float* row_var,
+                             const double* var_sum, int64_t var_rows, int32_t* row_k,
+                             int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                             int64_t bitmask_words, void* stream) {
+  return topk_select_adaptive_impl(scores, score_stride, B, Tq, Tkv, q_pos0, k_base, k_min,
+                                   k_max, row_var, var_sum, var_rows, row_k, indices, mask,
+                                   bitmask, bitmask_words, /*finite_rows=*/false, stream);
 }
 
 int gsa_adaptive_k_width(int k_max, int Tkv) { return k_max < Tkv ? k_max : Tkv; }
@@ -458,9 +473,9 @@ int gsa_indexer_topk_adaptive(const void* q, int64_t q_stride, const void* k, in
   if (rc) return rc;
   rc = gsa_row_variance(scores, stride, B, Tq, Tkv, q_pos0, row_var, var_sum, stream);
   if (rc) return rc;
-  return gsa_topk_select_adaptive(scores, stride, B, Tq, Tkv, q_pos0, k_base, k_min, k_max,
-                                  row_var, var_sum, static_cast<int64_t>(B) * Tq, row_k, indices,
-                                  mask, bitmask, bitmask_words, stream);
+  return topk_select_adaptive_impl(scores, stride, B, Tq, Tkv, q_pos0, k_base, k_min, k_max,
+                                   row_var, var_sum, static_cast<int64_t>(B) * Tq, row_k, indices,
+                                   mask, bitmask, bitmask_words, /*finite_rows=*/true, stream);
 }
 
 int gsa_masked_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,

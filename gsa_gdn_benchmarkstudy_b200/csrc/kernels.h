@@ -52,10 +52,12 @@ struct AdaptiveK {
 };
 
 // indices / mask rows are k_width slots wide (k_width >= the k of any row).
+// finite_rows: the caller guarantees that no score in a row's valid columns
+// is -inf (true for rows written by the indexer kernels).
 cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
                         int q_pos0, int k_sel, int k_width, const AdaptiveK& ad,
                         int32_t* indices, uint8_t* mask, uint32_t* bitmask,
-                        int64_t bitmask_words, cudaStream_t stream);
+                        int64_t bitmask_words, bool finite_rows, cudaStream_t stream);
 
 // Per-row population variance of the finite scores among columns
 // [0, min(q_pos0 + r + 1, Tkv)) into row_var[B * Tq], and their sum over all

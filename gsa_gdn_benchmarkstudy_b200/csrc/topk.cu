@@ -28,6 +28,8 @@
 // exact path: an MSB-first 11-bit radix select starting at the highest bit in
 // which the row's min and max keys differ, with candidate compaction, and a
 // warp-segmented emit.  Both paths implement the same selection rule.
+#include <type_traits>
+
 #include "kernels.h"
 
 namespace gsa {
@@ -41,6 +43,11 @@ static_assert(kTopkThreads >= 128 && kTopkThreads <= 1024 && (kTopkThreads & (kT
               "threads per row");
 constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kBins = 2048;   // 11-bit digits / histogram bins
+#ifndef GSA_TOPK_EMIT_GROUPS
+#define GSA_TOPK_EMIT_GROUPS 4
+#endif
+constexpr int kEmitGroups = GSA_TOPK_EMIT_GROUPS;  // 32-key groups per emit step (multiple of 4)
+static_assert(kEmitGroups % 4 == 0, "emit steps store whole 16-byte groups of words");
 constexpr int kDigitBits = 11;
 constexpr int kCandCap = 1024;  // candidate list capacity
 constexpr int kMaxWords = 2048; // bitmask words held in shared memory (Tkv <= 65536)
@@ -59,6 +66,7 @@ constexpr uint32_t kNegInfKey = 0x007FFFFFu;
 // shift, 0, 2047) for finite f (-1 for -inf), monotonic in the key order, and
 // after set_threshold(b) classify f as gt (bin > b) / eq (bin == b).
 struct OrdBins {
+  static constexpr bool kRawBits = false;
   uint32_t lo;
   int shift;
   int bstar = 0;
@@ -87,17 +95,22 @@ struct OrdBins {
 // order, every negative float (and -0.0) falls in bin 0 either way, so
 // bin(f) = clamp((max(bits, 0) - raw) >> shift, 0, 2047) as signed ints and
 // the gt / eq tests become two compares against the threshold bin's edges.
+// kFinite: the caller guarantees no -inf among the row's keys (the fused
+// indexer + top-k call: the indexer writes finite scores), so every key counts.
+template <bool kFinite>
 struct PosBins {
+  static constexpr bool kRawBits = true;
   int raw;
   int shift;
   int lo_edge = 0, hi_m1 = 0;
   static constexpr int kNegInfBits = static_cast<int>(0xFF800000u);
   __device__ PosBins(uint32_t raw_, int shift_) : raw(static_cast<int>(raw_)), shift(shift_) {}
-  // -inf is a negative float: bin 0, not counted
+  // -inf is a negative float: bin 0, not counted.  max(x, raw) - raw is
+  // max(max(x, 0) - raw, 0) for raw >= 0.
   __device__ __forceinline__ int hist_bin(float f, int& inc) const {
     const int x = __float_as_int(f);
-    inc = x != kNegInfBits ? 1 : 0;
-    return min(max(max(x, 0) - raw, 0) >> shift, kBins - 1);
+    inc = (kFinite || x != kNegInfBits) ? 1 : 0;
+    return min((max(x, raw) - raw) >> shift, kBins - 1);
   }
   // bin(f) > b  <=>  bits > hi_m1;  bin(f) >= b  <=>  bits >= lo_edge (b > 0).
   // A key of bin b exists (b holds the k-th largest), so lo_edge fits in int.
@@ -114,7 +127,7 @@ struct PosBins {
   }
 };
 
-struct TopkShared {
+struct alignas(16) TopkShared {
   int hist[kBins];
   uint32_t cand_key[kCandCap];
   int cand_idx[kCandCap];
@@ -208,6 +221,7 @@ __device__ __forceinline__ int adaptive_row_k(const AdaptiveK& ad, int64_t row) 
   return static_cast<int>(kf);
 }
 
+template <bool kFinite>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
     int k_fixed, int k_width, AdaptiveK ad, int32_t* __restrict__ indices,
@@ -320,11 +334,13 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
         const int bcount = sh.sh_bin;
         if (bcount > kCandCap) return false;
         bins.set_threshold(bstar);
-        // 4. bits for higher bins, candidates of the threshold bin
-        const int seg = ((nwords + kTopkWarps - 1) / kTopkWarps) * 32;
+        // 4. bits for higher bins, candidates of the threshold bin; G 32-key groups per
+        // step, whose loads are in flight together
+        constexpr int G = kEmitGroups;
+        // keys per warp: a multiple of one step (G groups of 32 keys), so a step's
+        // G words go out as G/4 16-byte stores
+        const int seg = ((nwords + G * kTopkWarps - 1) / (G * kTopkWarps)) * (G * 32);
         const int s0 = min(warp * seg, nwords * 32), s1 = min(s0 + seg, nwords * 32);
-        // four 32-key groups per step: their loads are in flight together
-        constexpr int G = 4;
         const float kNegInf = -__int_as_float(0x7F800000);
         auto emit_group = [&](int j0, float f) {
           bool gt, eq;
@@ -344,12 +360,55 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
           if (lane == 0) sh.bits[j0 >> 5] = hib;
         };
         const int full_end = s0 + max(0, min(s1, n) - s0) / (G * 32) * (G * 32);
-        for (int jb = s0; jb < full_end; jb += G * 32) {  // whole steps inside the row
-          float fg[G];
+        using BT = typename std::decay<decltype(bins)>::type;
+        if constexpr (BT::kRawBits) {
+          // whole steps inside the row: one compare per key for the bits, and the
+          // threshold-bin keys (a few per row) collected only in steps that have one
+          const int hi_m1 = bins.hi_m1, lo_edge = bins.lo_edge;
+          for (int jb = s0; jb < full_end; jb += G * 32) {
+            const float* p = srow + jb + lane;
+            int x[G];
 #pragma unroll
-          for (int g = 0; g < G; ++g) fg[g] = __ldg(srow + jb + g * 32 + lane);
+            for (int g = 0; g < G; ++g) x[g] = __float_as_int(__ldg(p + g * 32));
+            uint32_t w[G];
+            bool in = false;
 #pragma unroll
-          for (int g = 0; g < G; ++g) emit_group(jb + g * 32, fg[g]);
+            for (int g = 0; g < G; ++g) {
+              w[g] = __ballot_sync(0xFFFFFFFFu, x[g] > hi_m1);
+              in |= x[g] >= lo_edge && x[g] <= hi_m1;
+            }
+            if (lane == 0) {
+#pragma unroll
+              for (int q4 = 0; q4 < G / 4; ++q4)
+                *reinterpret_cast<uint4*>(&sh.bits[(jb >> 5) + 4 * q4]) =
+                    make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+            }
+            if (__any_sync(0xFFFFFFFFu, in)) {
+#pragma unroll
+              for (int g = 0; g < G; ++g) {
+                const bool eq = x[g] >= lo_edge && x[g] <= hi_m1 && x[g] != BT::kNegInfBits;
+                const uint32_t eqb = __ballot_sync(0xFFFFFFFFu, eq);
+                if (eqb) {
+                  int base = 0;
+                  if (lane == 0) base = atomicAdd(&sh.n_cand, __popc(eqb));
+                  base = __shfl_sync(0xFFFFFFFFu, base, 0);
+                  if (eq) {
+                    const int c = base + __popc(eqb & lt_mask);
+                    sh.cand_key[c] = ord_key(__int_as_float(x[g]));
+                    sh.cand_idx[c] = jb + g * 32 + lane;
+                  }
+                }
+              }
+            }
+          }
+        } else {
+          for (int jb = s0; jb < full_end; jb += G * 32) {  // whole steps inside the row
+            float fg[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) fg[g] = __ldg(srow + jb + g * 32 + lane);
+#pragma unroll
+            for (int g = 0; g < G; ++g) emit_group(jb + g * 32, fg[g]);
+          }
         }
         for (int j0 = full_end; j0 < s1; j0 += 32) {  // ragged tail, checked
           const int j = j0 + lane;
@@ -409,7 +468,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
         }
         return true;
       };
-      done = lo >= 0x80000000u ? fast(PosBins(lo - 0x80000000u, shift)) : fast(OrdBins(lo, shift));
+      done = lo >= 0x80000000u ? fast(PosBins<kFinite>(lo - 0x80000000u, shift))
+                               : fast(OrdBins(lo, shift));
     }
     __syncthreads();
   }
@@ -679,12 +739,17 @@ __global__ void __launch_bounds__(kSumThreads) var_sum_kernel(const float* __res
 cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
                         int q_pos0, int k_sel, int k_width, const AdaptiveK& ad,
                         int32_t* indices, uint8_t* mask, uint32_t* bitmask,
-                        int64_t bitmask_words, cudaStream_t stream) {
+                        int64_t bitmask_words, bool finite_rows, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * Tq;
   if (rows == 0) return cudaSuccess;
-  topk_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-      scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
-      bitmask_words);
+  if (finite_rows)
+    topk_kernel<true><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+        scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
+        bitmask_words);
+  else
+    topk_kernel<false><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+        scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
+        bitmask_words);
   return cudaGetLastError();
 }
 
