@@ -342,8 +342,11 @@ def test_gather_attention_vs_oracle(dtype):
 
 # ──────────────────────────────────────────────────────────── fused indexer + top-k
 @pytest.mark.parametrize("B,Tq,Tkv,q_pos0,k_sel", [(2, 160, 160, 0, 48), (1, 700, 1500, 800, 256),
-                                                   (1, 2048, 2048, 0, 2048)])
+                                                   (1, 2048, 2048, 0, 2048),
+                                                   (1, 64, 40000, 39936, 2048)])  # long rows
 def test_indexer_topk_matches_separate_calls(B, Tq, Tkv, q_pos0, k_sel):
+    """The fused call (rows known finite) selects exactly as indexer + the standalone
+    selector (which also handles -inf), for short and for long (32K+ key) rows."""
     q, k, w, bias = _indexer_inputs(B, Tq, Tkv, torch.bfloat16, seed=Tq)
     qc, kc, wc, bc = q.cuda(), k.cuda(), w.cuda(), bias.cuda()
     scores = ops.indexer_scores(qc, kc, wc, bc, 0.125, q_pos0=q_pos0, tkv=Tkv, fill_upper=False)
