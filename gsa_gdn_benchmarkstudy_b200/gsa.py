@@ -597,9 +597,17 @@ class GatedSparseAttention(nn.Module):
             unit = tiles / (n - 1)
             cuts = [0.0] + [unit * (i - 0.5) for i in range(1, n)] + [float(tiles)]
         bounds = sorted({min(T, 128 * int(round(c))) for c in cuts} | {0, T})
+        # the copies in go first: everything else waits on them
+        x_dev = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
+        done_in = []
+        for r0, r1 in zip(bounds[:-1], bounds[1:]):
+            with torch.cuda.stream(h2d):
+                x_dev[:, r0:r1].copy_(x_host[:, r0:r1], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                done_in.append(e)
         w, bias = self._get_fused_weight()
         cos, sin = self.rotary_emb(T, dev, x_host.dtype)
-        x_dev = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
         proj = torch.empty(1, T, self._proj_padded, device=dev, dtype=x_host.dtype)
         q = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
         k = torch.empty_like(q)
@@ -612,13 +620,6 @@ class GatedSparseAttention(nn.Module):
         bm_flat = (torch.empty(sum(bm_sizes), device=dev, dtype=torch.int32) if bf16_tc
                    else None)
         bm_offs = [sum(bm_sizes[:i]) for i in range(len(bm_sizes))]
-        done_in = []
-        for r0, r1 in zip(bounds[:-1], bounds[1:]):
-            with torch.cuda.stream(h2d):
-                x_dev[:, r0:r1].copy_(x_host[:, r0:r1], non_blocking=True)
-                e = torch.cuda.Event()
-                e.record(h2d)
-                done_in.append(e)
         parts_all = self.split(proj)
         side = self._side_stream(dev)
         side.wait_stream(compute)  # the buffers above come from the current stream's pool
