@@ -9,7 +9,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from gsa_gdn_benchmarkstudy_b200.sharding import (causal_row_cost, gather_batch, gather_rows,
-                                                  zigzag_blocks)
+                                                  unshard_rows, zigzag_blocks, zigzag_order)
 
 
 @pytest.mark.parametrize("T,world", [(16384, 1), (16384, 2), (16384, 8), (65536, 8), (64, 4)])
@@ -35,6 +35,18 @@ def test_zigzag_covers_every_row_once_and_balances(T, world):
 def test_zigzag_rejects_ragged_lengths():
     with pytest.raises(ValueError):
         zigzag_blocks(1000, 3, 0)
+
+
+@pytest.mark.parametrize("T,world", [(64, 1), (64, 2), (4096, 8), (96, 3)])
+def test_zigzag_order_unshards_a_rank_major_gather(T, world):
+    """zigzag_order maps every sequence row to its row in the rank-major
+    concatenation of the ranks' local shards; unshard_rows applies it."""
+    full = torch.arange(T * 2, dtype=torch.float32).view(1, T, 2)
+    shards = torch.stack([torch.cat([full[0, s:e] for s, e in zigzag_blocks(T, world, r)])
+                          for r in range(world)])            # [world, T/world, 2]
+    order = zigzag_order(T, world, torch.device("cpu"))
+    assert sorted(order.tolist()) == list(range(T))
+    assert torch.equal(unshard_rows(shards, order), full)
 
 
 def _free_port():
