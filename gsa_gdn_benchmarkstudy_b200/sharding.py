@@ -179,14 +179,26 @@ class ShardedGSA:
 
     def _forward_rows(self, x_loc: torch.Tensor, gather: bool = True) -> torch.Tensor:
         m = self.model
-        T, D, H = self.T, m.hidden_size, m.num_heads
-        dev = x_loc.device
-        order = self._row_order(dev)
         proj = m.project(x_loc)
+        outs = self._rows_from_projection(proj, x_loc.dtype)
+        out_local = F.linear(torch.cat(outs, dim=1), m.o_proj.weight)
+        return (gather_rows(out_local, self.T, self.group, self._row_order(x_loc.device))
+                if gather else out_local)
+
+    def _rows_from_projection(self, proj: torch.Tensor, dtype, per_block=None) -> list:
+        """Everything after the projection GEMM of this rank's rows: gathers,
+        RoPE + value gate, selection and attention.  Returns the gated attention
+        output of each block ([1, n, D], in the order of ``self.blocks``); with
+        ``per_block(i, o, n, attn)`` that callback receives each block as soon as
+        it is computed."""
+        m = self.model
+        T, H = self.T, m.num_heads
+        dev = proj.device
+        order = self._row_order(dev)
         parts = m.split(proj)
         # the selection needs only the indexer keys of the whole sequence (2 MB at T=16K)
         ik_full = gather_rows(parts["ik"].contiguous(), T, self.group, order)
-        cos, sin = m.rotary_emb(T, dev, x_loc.dtype)
+        cos, sin = m.rotary_emb(T, dev, dtype)
         pos = self._positions(dev)
         q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
                                  sin.index_select(0, pos), H, v_src=parts["v"],
@@ -220,11 +232,13 @@ class ShardedGSA:
         wv.wait()
         k_full = unshard_rows(gk, order)
         v_full = unshard_rows(gv, order)
-        outs = [m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e], q[:, o:o + n], q_pos0=s)
-                for (pb, s, e, o, n), sel in zip(blocks, sels)]
-        attn = torch.cat(outs, dim=1)
-        out_local = F.linear(attn, m.o_proj.weight)
-        return gather_rows(out_local, T, self.group, order) if gather else out_local
+        outs = []
+        for i, ((pb, s, e, o, n), sel) in enumerate(zip(blocks, sels)):
+            a = m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e], q[:, o:o + n], q_pos0=s)
+            if per_block is not None:
+                per_block(i, o, n, a)
+            outs.append(a)
+        return outs
 
     def forward_host(self, x_local_host: torch.Tensor) -> torch.Tensor:
         """This rank's input share from pinned host memory -> device, sharded forward,
@@ -232,11 +246,50 @@ class ShardedGSA:
 
         Rows come back in the order of ``local_input`` (this rank's blocks, or
         its sequences); no output all-gather is needed, so each rank copies
-        back 1/P of the output."""
+        back 1/P of the output.  With row shards the copies overlap the work:
+        each block's rows are projected as soon as they have arrived, and each
+        block's output rows are copied back while the next block computes."""
         dev = torch.device("cuda", torch.cuda.current_device())
-        out = self._forward(x_local_host.to(dev, non_blocking=True), gather=False)
-        if self._host_out is None or self._host_out.shape != out.shape:
-            self._host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        self._host_out.copy_(out, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        if not x_local_host.is_pinned():
+            x_local_host = x_local_host.pin_memory()
+        if self._host_out is None or self._host_out.shape != x_local_host.shape:
+            self._host_out = torch.empty(x_local_host.shape,
+                                         dtype=x_local_host.dtype).pin_memory()
+        if self.mode == "batch":
+            out = self._forward(x_local_host.to(dev, non_blocking=True), gather=False)
+            self._host_out.copy_(out, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            return self._host_out
+        m = self.model
+        compute = torch.cuda.current_stream(dev)
+        h2d, d2h = m._copy_streams(dev)
+        h2d.wait_stream(compute)  # device buffers below come from the current stream's pool
+        _, Tl, D = x_local_host.shape
+        x_dev = torch.empty(1, Tl, D, device=dev, dtype=x_local_host.dtype)
+        arrived, off = [], 0
+        for s, e in self.blocks:
+            with torch.cuda.stream(h2d):
+                x_dev[:, off:off + e - s].copy_(x_local_host[:, off:off + e - s],
+                                                non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+            arrived.append((ev, off, e - s))
+            off += e - s
+        w, bias = m._get_fused_weight()
+        proj = torch.empty(1, Tl, m._proj_padded, device=dev, dtype=x_local_host.dtype)
+        for ev, o, n in arrived:
+            compute.wait_event(ev)
+            torch.addmm(bias, x_dev[0, o:o + n], w.t(), out=proj[0, o:o + n])
+        y = torch.empty(1, Tl, D, device=dev, dtype=x_local_host.dtype)
+
+        def block_out(i, o, n, a):
+            torch.mm(a[0], m.o_proj.weight.t(), out=y[0, o:o + n])
+            d2h.wait_stream(compute)
+            with torch.cuda.stream(d2h):
+                self._host_out[:, o:o + n].copy_(y[:, o:o + n], non_blocking=True)
+
+        self._rows_from_projection(proj, x_local_host.dtype, per_block=block_out)
+        y.record_stream(d2h)
+        compute.wait_stream(d2h)
+        d2h.synchronize()
         return self._host_out

@@ -74,15 +74,25 @@ def test_batch_sharded_matches_unsharded(group):
 @pytest.mark.parametrize("name", ["small_bf16", "tiny_bf16"])
 def test_forward_host_returns_this_ranks_rows(group, name):
     """forward_host: pinned host share in, this rank's output rows out (in the
-    order of local_input), equal to those rows of the device-resident result."""
+    order of local_input), equal to those rows of the device-resident result.
+    With row shards it projects and outputs block by block, so its GEMMs may
+    round differently from the whole-share ones (bf16 output bound); with batch
+    shards it runs the same GEMMs (bit-equal)."""
     cfg = TEST_CONFIGS[name]
     m = _model(cfg)
     x = make_input(cfg)
     runner = ShardedGSA(m, group, T=cfg.T, B=cfg.B)
     full = runner(runner.local_input(x.cuda())).cpu()
-    got = runner.forward_host(runner.local_input(x).pin_memory())
-    assert not got.is_cuda
-    assert torch.equal(got, runner.local_input(full))
+    for _ in range(2):  # the second call reuses the pinned output and the streams
+        got = runner.forward_host(runner.local_input(x).pin_memory())
+        assert not got.is_cuda
+        ref = runner.local_input(full)
+        if runner.mode == "batch":
+            assert torch.equal(got, ref)
+        else:
+            err = (got.float() - ref.float()).abs().max().item()
+            rel = ((got.float() - ref.float()).norm() / ref.float().norm()).item()
+            assert err < 2e-2 and rel < 1e-2, (err, rel)
 
 
 @pytest.mark.parametrize("name", ["small_bf16", "tiny_bf16"])
