@@ -591,11 +591,12 @@ class GatedSparseAttention(nn.Module):
         tiles = (T + 127) // 128
         n = max(1, min(chunks, tiles))
         # block bounds on 128-row tiles: half-size first and last blocks
+        f0, fl = getattr(self, "_host_edges", (0.5, 0.5))
         if n <= 2:
             cuts = [tiles * i / n for i in range(n + 1)]
         else:
-            unit = tiles / (n - 1)
-            cuts = [0.0] + [unit * (i - 0.5) for i in range(1, n)] + [float(tiles)]
+            unit = tiles / (n - 2 + f0 + fl)
+            cuts = [0.0] + [unit * (i - 1 + f0) for i in range(1, n)] + [float(tiles)]
         bounds = sorted({min(T, 128 * int(round(c))) for c in cuts} | {0, T})
         # the copies in go first: everything else waits on them
         x_dev = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)

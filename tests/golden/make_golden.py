@@ -129,7 +129,8 @@ def make_adaptive(reference: Path) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of nirmalpratheep/GSA_GDN_BenchmarkStudy (read only)")
     ap.add_argument("--parts", default="all", choices=("all", "adaptive"),
                     help="'adaptive' regenerates only adaptive_k.pt (needs the tiny fixtures)")
     args = ap.parse_args()
