@@ -46,8 +46,11 @@ constexpr int kBins = 2048;   // 11-bit digits / histogram bins
 // 32-key groups per emit step, whose loads are in flight together.  Measured
 // top-k times for 4 / 8 / 16 groups: at T=64K, where the emit pass reads the
 // score rows back from DRAM, 3.66 / 3.34 / 3.09 ms; at T=16K, where they come
-// from L2, 0.280 / 0.278 / 0.289 ms.
-constexpr int kEmitGroups = 16;
+// from L2, 0.280 / 0.278 / 0.289 ms.  Key ranges of kLongKeyRange or more take
+// the long step, shorter ones the short step (one kernel instance each).
+constexpr int kEmitShort = 4;
+constexpr int kEmitLong = 16;
+constexpr int kLongKeyRange = 32768;
 constexpr int kDigitBits = 11;
 constexpr int kCandCap = 1024;  // candidate list capacity
 constexpr int kMaxWords = 2048; // bitmask words held in shared memory (Tkv <= 65536)
@@ -221,7 +224,7 @@ __device__ __forceinline__ int adaptive_row_k(const AdaptiveK& ad, int64_t row) 
   return static_cast<int>(kf);
 }
 
-template <bool kFinite>
+template <bool kFinite, int kGroups>
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
     int k_fixed, int k_width, AdaptiveK ad, int32_t* __restrict__ indices,
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
         bins.set_threshold(bstar);
         // 4. bits for higher bins, candidates of the threshold bin; G 32-key groups per
         // step, whose loads are in flight together
-        constexpr int G = kEmitGroups;
+        constexpr int G = kGroups;
         // keys per warp: a multiple of one step, so a step's words go out as
         // 16-byte stores
         const int seg = ((nwords + G * kTopkWarps - 1) / (G * kTopkWarps)) * (G * 32);
@@ -744,14 +747,13 @@ cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq
                         int64_t bitmask_words, bool finite_rows, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * Tq;
   if (rows == 0) return cudaSuccess;
-  if (finite_rows)
-    topk_kernel<true><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-        scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
-        bitmask_words);
-  else
-    topk_kernel<false><<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-        scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
-        bitmask_words);
+  auto kernel = finite_rows ? (Tkv >= kLongKeyRange ? topk_kernel<true, kEmitLong>
+                                                    : topk_kernel<true, kEmitShort>)
+                            : (Tkv >= kLongKeyRange ? topk_kernel<false, kEmitLong>
+                                                    : topk_kernel<false, kEmitShort>);
+  kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+      scores, score_stride, Tq, Tkv, q_pos0, k_sel, k_width, ad, indices, mask, bitmask,
+      bitmask_words);
   return cudaGetLastError();
 }
 
