@@ -119,6 +119,16 @@ def test_forward_host_odd_length_fp32():
     check_fp32(got, m(x.cuda()))
 
 
+def test_forward_host_default_blocks_short_and_long():
+    """Default block count: one block for T < 4096 (small_bf16, T = 1024), two
+    for cfg2 (T = 4096); both equal the device-resident forward."""
+    for cfg in (TEST_CONFIGS["small_bf16"], CONFIGS["cfg2"]):
+        m = make_model(cfg)
+        x = make_input(cfg)
+        got = m.forward_host(x.pin_memory())
+        check_bf16(got, m(x.cuda()))
+
+
 def test_forward_is_deterministic():
     cfg = TEST_CONFIGS["small_bf16"]
     m = make_model(cfg)
