@@ -20,10 +20,10 @@ from .gsa import (  # noqa: F401
     ValueGate,
     apply_rotary_pos_emb,
 )
-from .ops import fused_gated_indexer, fused_sparse_attention  # noqa: F401
+from .ops import fused_gated_indexer, fused_sparse_attention, sparse_attention_ref  # noqa: F401
 
 __all__ = [
     "GatedSparseAttention", "GatedLightningIndexer", "AdaptiveTopKSelector", "ValueGate",
     "OutputGate", "RotaryEmbedding", "apply_rotary_pos_emb", "fused_gated_indexer",
-    "fused_sparse_attention",
+    "fused_sparse_attention", "sparse_attention_ref",
 ]

@@ -8,6 +8,7 @@ The op-level functions of the reference are mirrored with the same names and
 argument meaning:
   * ``fused_gated_indexer``  — gsa_triton/gsa_opt.py:143-176
   * ``fused_sparse_attention`` — gsa_triton/gsa_opt.py:349-383
+  * ``sparse_attention_ref`` — gsa_triton/gsa_ref.py:202-238 (same kernel)
   * ``apply_rotary_pos_emb`` — gsa_triton/gsa_ref.py:35-40
 """
 from __future__ import annotations
@@ -415,6 +416,14 @@ def gather_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
 
 def fused_sparse_attention(q, k, v, indices, mask, scale: float) -> torch.Tensor:
     """Drop-in for gsa_opt.fused_sparse_attention: [B, T, H, d] in q's dtype."""
+    return gather_attention(q, k, v, indices, mask, scale)
+
+
+def sparse_attention_ref(q, k, v, indices, mask, scale: float) -> torch.Tensor:
+    """Drop-in for gsa_ref.sparse_attention_ref (gsa_ref.py:202-238), same arguments:
+    q [B, T, H, d], k / v [B, T_kv, H, d], indices / mask [B, T, k_sel].  Runs the
+    index-gather kernel; a row whose mask is all False comes out as zeros, as the
+    reference's nan_to_num makes it."""
     return gather_attention(q, k, v, indices, mask, scale)
 
 

@@ -338,6 +338,10 @@ def test_gather_attention_vs_oracle(dtype):
     assert torch.equal(got[0, 7], torch.zeros_like(got[0, 7]))
     atol = 2e-2 if dtype == torch.bfloat16 else 1e-5
     _check_close(got, ref, atol=atol)
+    # the gsa_ref.py name of the same op gives the same result
+    from gsa_gdn_benchmarkstudy_b200 import sparse_attention_ref
+    again = sparse_attention_ref(q.cuda(), k.cuda(), v.cuda(), idx.cuda(), mask.cuda(), scale)
+    assert torch.equal(again.cpu(), got)
 
 
 # ──────────────────────────────────────────────────────────── fused indexer + top-k
