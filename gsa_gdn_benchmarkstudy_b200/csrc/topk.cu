@@ -258,6 +258,20 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     }
     return;
   }
+  if (kFinite && n <= k_sel) {
+    // every key of the row is selected (finite rows: no -inf to leave out), so
+    // the selection is columns [0, n) without reading a score
+    if (brow) {
+      const int full = n >> 5, rem = n & 31;
+      for (int64_t w = tid; w < bm_words; w += kTopkThreads)
+        brow[w] = w < full ? 0xFFFFFFFFu : (w == full && rem ? (1u << rem) - 1u : 0u);
+    }
+    for (int s = tid; s < k_width; s += kTopkThreads) {
+      if (irow) irow[s] = min(s, Tkv - 1);  // s itself below n; filler above
+      if (mrow) mrow[s] = s < n ? 1 : 0;
+    }
+    return;
+  }
 
   // =================================================================== fast path
   bool done = false;
