@@ -245,6 +245,29 @@ class OutputGate(nn.Module):
         return ops.output_gate(output, self.gate_proj(x)).view(B, T, H, d)
 
 
+# ── Row blocks of the host-buffer forward ───────────────────────────────────
+
+def host_row_block_bounds(T: int, chunks: Optional[int] = None) -> list:
+    """Block edges [0, r1, ..., T] of ``forward_host`` for one sequence of T rows.
+
+    Edges sit on 128-row tiles (the kernels' query tile) except the last, and
+    the first and last blocks are half the size of the others: nothing overlaps
+    the first copy in or the last copy out.  By default there are at most 5
+    blocks and at most one per 2048 rows: below that the per-block launches
+    cost more than the overlap saves (T=4096: 0.96 ms with 2 blocks, 1.72 ms
+    with 5)."""
+    tiles = (T + 127) // 128
+    if chunks is None:
+        chunks = max(1, min(5, T // 2048))
+    n = max(1, min(chunks, tiles))
+    if n <= 2:
+        cuts = [tiles * i / n for i in range(n + 1)]
+    else:
+        unit = tiles / (n - 1)
+        cuts = [0.0] + [unit * (i - 0.5) for i in range(1, n)] + [float(tiles)]
+    return sorted({min(T, 128 * int(round(c))) for c in cuts} | {0, T})
+
+
 # ── Main module ────────────────────────────────────────────────────────────
 
 class GatedSparseAttention(nn.Module):
@@ -589,20 +612,7 @@ class GatedSparseAttention(nn.Module):
         block c's attention leaves idle."""
         _, T, D = x_host.shape
         H = self.num_heads
-        tiles = (T + 127) // 128
-        # by default at most one block per 2048 rows: below that the per-block
-        # launches cost more than the overlap saves (T=4096: 0.96 ms with 2
-        # blocks, 1.72 ms with 5)
-        if chunks is None:
-            chunks = max(1, min(5, T // 2048))
-        n = max(1, min(chunks, tiles))
-        # block bounds on 128-row tiles: half-size first and last blocks
-        if n <= 2:
-            cuts = [tiles * i / n for i in range(n + 1)]
-        else:
-            unit = tiles / (n - 1)
-            cuts = [0.0] + [unit * (i - 0.5) for i in range(1, n)] + [float(tiles)]
-        bounds = sorted({min(T, 128 * int(round(c))) for c in cuts} | {0, T})
+        bounds = host_row_block_bounds(T, chunks)
         # the copies in go first: everything else waits on them
         x_dev = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
         done_in = []
