@@ -58,6 +58,7 @@ constexpr int kAtTileBytes = kAtBM * kAtD * 2;  // 32 KB: two 128x64 swizzled bo
 constexpr int kAtBoxBytes = kAtTileBytes / 2;   // 16 KB
 constexpr int kAtThreads = 384;
 constexpr int kAtTmemCols = 512;
+constexpr int kAtPairGroup = 4;  // (batch, head) pairs scheduled together, heavy tiles first
 constexpr float kRescaleLog2 = 8.0f;            // p may reach 2^8 before m is raised
 constexpr long long kDrainCycles = 200000000LL; // ~0.1 s: in-flight copies/MMAs after an abort
 // Register split (setmaxnreg): the launch gives 384 threads x 168 registers;
@@ -130,9 +131,14 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int n_qt = (a.Tq + kAtBM - 1) / kAtBM;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // heavy tiles first
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  // Grid (pairs per group, query tiles, groups): the blocks of a group of
+  // kAtPairGroup (batch, head) pairs are dispatched heavy tiles first across
+  // the whole group, so the last wave holds light tiles, while only the
+  // group's K/V (a few MB per pair) is live in L2 at a time.
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.y);
+  const int pair = static_cast<int>(blockIdx.z * gridDim.x + blockIdx.x);
+  const int h = pair % a.H;
+  const int b = pair / a.H;
   const int row0 = qt * kAtBM;
   const int maxpos = a.q_pos0 + min(row0 + kAtBM - 1, a.Tq - 1);
   const int nt = min((a.Tkv + kAtBN - 1) / kAtBN, maxpos / kAtBN + 1);
@@ -465,7 +471,10 @@ cudaError_t launch_masked_attention(const CUtensorMap& qmap, const CUtensorMap& 
     attr_set[dev] = true;
   }
   const int n_qt = (a.Tq + kAtBM - 1) / kAtBM;
-  dim3 grid(n_qt, a.H, a.B);
+  const int pairs = a.B * a.H;
+  const int group = pairs % kAtPairGroup == 0 ? kAtPairGroup : (pairs % 2 == 0 ? 2 : 1);
+  if (n_qt > 65535 || pairs / group > 65535) return cudaErrorInvalidConfiguration;
+  dim3 grid(group, n_qt, pairs / group);
   masked_attn_kernel<<<grid, kAtThreads, kAtSmemBytes, stream>>>(qmap, kmap, vmap, a);
   return cudaGetLastError();
 }
