@@ -15,6 +15,7 @@ from .gsa import (  # noqa: F401
     AdaptiveTopKSelector,
     GatedLightningIndexer,
     GatedSparseAttention,
+    GraphedForward,
     OutputGate,
     RotaryEmbedding,
     ValueGate,
@@ -23,7 +24,7 @@ from .gsa import (  # noqa: F401
 from .ops import fused_gated_indexer, fused_sparse_attention, sparse_attention_ref  # noqa: F401
 
 __all__ = [
-    "GatedSparseAttention", "GatedLightningIndexer", "AdaptiveTopKSelector", "ValueGate",
-    "OutputGate", "RotaryEmbedding", "apply_rotary_pos_emb", "fused_gated_indexer",
+    "GatedSparseAttention", "GraphedForward", "GatedLightningIndexer", "AdaptiveTopKSelector",
+    "ValueGate", "OutputGate", "RotaryEmbedding", "apply_rotary_pos_emb", "fused_gated_indexer",
     "fused_sparse_attention", "sparse_attention_ref",
 ]

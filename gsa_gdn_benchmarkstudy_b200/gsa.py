@@ -489,9 +489,12 @@ class GatedSparseAttention(nn.Module):
         return ws, (bm[:n_words].view(shape) if want_bitmask else None)
 
     def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        """The stream of indexer + top-k.  It has high priority: that branch is
+        the longer of the two that follow the projection (RoPE + gates is the
+        other), so its blocks go first whenever both have blocks waiting."""
         s = self._streams.get(device)
         if s is None:
-            s = torch.cuda.Stream(device=device)
+            s = torch.cuda.Stream(device=device, priority=-1)
             self._streams[device] = s
         return s
 
@@ -499,11 +502,21 @@ class GatedSparseAttention(nn.Module):
                 ) -> torch.Tensor:
         return self._forward_impl(x)
 
+    def graphed(self, shape, dtype: Optional[torch.dtype] = None, device=None,
+                warmup: int = 2) -> "GraphedForward":
+        """The forward for inputs of ``shape`` captured as a CUDA graph
+        (``GraphedForward``); ``dtype`` defaults to the parameters' dtype."""
+        p = self.q_proj.weight
+        return GraphedForward(self, shape, p.dtype if dtype is None else dtype,
+                              p.device if device is None else device, warmup)
+
     def _forward_impl(self, x: torch.Tensor, var_reduce=None,
-                      var_rows: Optional[int] = None) -> torch.Tensor:
+                      var_rows: Optional[int] = None,
+                      side: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """``forward``; ``var_reduce`` / ``var_rows`` as in ``select_blocks`` let a
         caller whose batch spans several processes average adaptive k's row
-        variances over all of it."""
+        variances over all of it.  ``side`` replaces the module's side stream
+        (a captured graph keeps its own, and with it its own scratch)."""
         if not x.is_cuda:
             raise RuntimeError("gsa_b200.GatedSparseAttention runs on CUDA only (no CPU path)")
         if x.dtype not in (torch.bfloat16, torch.float32):
@@ -519,7 +532,7 @@ class GatedSparseAttention(nn.Module):
         # indexer + top-k (tensor/MUFU-bound) run beside RoPE + value gate
         # (HBM-bound); the attention waits for both.
         main = torch.cuda.current_stream(x.device)
-        side = self._side_stream(x.device)
+        side = self._side_stream(x.device) if side is None else side
         side.wait_stream(main)
         with torch.cuda.stream(side):
             sel = self.select_blocks([(parts, parts["ik"], 0, T)], var_reduce, var_rows)[0]
@@ -688,3 +701,60 @@ class GatedSparseAttention(nn.Module):
         compute.wait_stream(d2h)
         d2h.synchronize()
         return out
+
+
+# ── CUDA-graph replay ──────────────────────────────────────────────────────
+
+class GraphedForward:
+    """``module(x)`` for one input shape, captured once as a CUDA graph.
+
+    No counterpart in the reference, which launches every step from Python.
+    One forward issues about a dozen kernels and copies on two streams, plus
+    the Python around them; for short sequences (T of a few thousand and
+    below) that host work, not the GPU, sets the step time.  A replay issues
+    the whole forward as one graph launch on the caller's current stream.
+
+    The graph owns its input buffer ``x`` and its output ``out``: a call copies
+    its argument into ``x`` (skip it by writing ``x`` directly and calling with
+    no argument), replays, and returns ``out``, which the next replay
+    overwrites.  The captured side stream is private to the graph, and so is
+    the indexer/top-k scratch, so replays and eager calls of the module do not
+    share buffers.  Weights are captured by address: after changing them call
+    ``module.fuse_projections()`` and capture again.
+    """
+
+    def __init__(self, module: "GatedSparseAttention", shape, dtype: torch.dtype,
+                 device=None, warmup: int = 2):
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("GraphedForward needs a CUDA device")
+        if module._stage_events is not None:
+            raise RuntimeError("per-stage timing events cannot be captured; disable them first")
+        self.module = module
+        self.x = torch.zeros(tuple(shape), dtype=dtype, device=device)
+        self._main = torch.cuda.Stream(device=device)
+        self._side = torch.cuda.Stream(device=device, priority=-1)  # as the module's side stream
+        self._main.wait_stream(torch.cuda.current_stream(device))
+        with torch.no_grad(), torch.cuda.stream(self._main):
+            # eager warm-up on the capture streams: builds the fused weight,
+            # the rotary tables and this graph's scratch outside the graph pool
+            for _ in range(max(1, warmup)):
+                module._forward_impl(self.x, side=self._side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph, stream=self._main):
+            self.out = module._forward_impl(self.x, side=self._side)
+        # the graph reads these by address: hold them even if the module later
+        # replaces its caches (new sequence length, dtype, re-fused weights)
+        self._held = (module._fused_weight, module._fused_bias,
+                      getattr(module.indexer, "_bias32", None),
+                      getattr(module.rotary_emb, "_tables", None), dict(module._workspaces))
+
+    def __call__(self, x: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x is not None:
+            if x.shape != self.x.shape or x.dtype != self.x.dtype:
+                raise RuntimeError(f"captured for {tuple(self.x.shape)} {self.x.dtype}, "
+                                   f"got {tuple(x.shape)} {x.dtype}")
+            self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.out

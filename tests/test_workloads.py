@@ -65,6 +65,13 @@ def test_forward_refuses_cpu_tensors():
         m(make_input(cfg))
 
 
+def test_graphed_forward_refuses_cpu_device():
+    cfg = TEST_CONFIGS["tiny_fp32"]
+    m = GatedSparseAttention(**cfg.module_kwargs())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m.graphed((cfg.B, cfg.T, cfg.D), device="cpu")
+
+
 def test_fused_projection_layout():
     cfg = TEST_CONFIGS["tiny_fp32"]
     m = init_weights_(GatedSparseAttention(**cfg.module_kwargs()))
