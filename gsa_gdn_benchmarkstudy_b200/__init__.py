@@ -16,6 +16,7 @@ from .gsa import (  # noqa: F401
     GatedLightningIndexer,
     GatedSparseAttention,
     GraphedForward,
+    GraphedForwardHost,
     OutputGate,
     RotaryEmbedding,
     ValueGate,
@@ -24,7 +25,7 @@ from .gsa import (  # noqa: F401
 from .ops import fused_gated_indexer, fused_sparse_attention, sparse_attention_ref  # noqa: F401
 
 __all__ = [
-    "GatedSparseAttention", "GraphedForward", "GatedLightningIndexer", "AdaptiveTopKSelector",
-    "ValueGate", "OutputGate", "RotaryEmbedding", "apply_rotary_pos_emb", "fused_gated_indexer",
+    "GatedSparseAttention", "GraphedForward", "GraphedForwardHost", "GatedLightningIndexer",
+    "AdaptiveTopKSelector", "ValueGate", "OutputGate", "RotaryEmbedding", "apply_rotary_pos_emb", "fused_gated_indexer",
     "fused_sparse_attention", "sparse_attention_ref",
 ]

@@ -247,18 +247,22 @@ class OutputGate(nn.Module):
 
 # ── Row blocks of the host-buffer forward ───────────────────────────────────
 
-def host_row_block_bounds(T: int, chunks: Optional[int] = None) -> list:
+def host_row_block_bounds(T: int, chunks: Optional[int] = None, graphed: bool = False) -> list:
     """Block edges [0, r1, ..., T] of ``forward_host`` for one sequence of T rows.
 
     Edges sit on 128-row tiles (the kernels' query tile) except the last, and
     the first and last blocks are half the size of the others: nothing overlaps
     the first copy in or the last copy out.  By default there are at most 5
-    blocks and at most one per 2048 rows: below that the per-block launches
-    cost more than the overlap saves (T=4096: 0.96 ms with 2 blocks, 1.72 ms
-    with 5)."""
+    blocks and at most one per 2048 rows: below that Python's issue of each
+    block's launches costs more than the overlap saves (T=4096: 0.96 ms with 2
+    blocks, 1.72 ms with 5).  Replayed from a CUDA graph (``graphed``) nothing
+    waits on Python, and finer blocks start the computation sooner behind the
+    copies in: at most 9 blocks and one per 1024 rows (T=16384: 2.95 ms with 5
+    blocks, 2.78 ms with 9, 2.84 ms with 12; T=4096: 0.73 ms with 2, 0.66 ms
+    with 4, 0.72 ms with 6)."""
     tiles = (T + 127) // 128
     if chunks is None:
-        chunks = max(1, min(5, T // 2048))
+        chunks = max(1, min(9, T // 1024)) if graphed else max(1, min(5, T // 2048))
     n = max(1, min(chunks, tiles))
     if n <= 2:
         cuts = [tiles * i / n for i in range(n + 1)]
@@ -549,6 +553,14 @@ class GatedSparseAttention(nn.Module):
         _nvtx_pop()
         return out
 
+    def graphed_host(self, shape, dtype: Optional[torch.dtype] = None, device=None,
+                     chunks: Optional[int] = None, warmup: int = 2) -> "GraphedForwardHost":
+        """``forward_host`` for host inputs of ``shape`` captured as a CUDA graph
+        (``GraphedForwardHost``); ``dtype`` defaults to the parameters' dtype."""
+        p = self.q_proj.weight
+        return GraphedForwardHost(self, shape, p.dtype if dtype is None else dtype,
+                                  p.device if device is None else device, chunks, warmup)
+
     # ------------------------------------------------------- host-buffer forward
     def forward_host(self, x_host: torch.Tensor, out: Optional[torch.Tensor] = None,
                      chunks: Optional[int] = None) -> torch.Tensor:
@@ -585,6 +597,17 @@ class GatedSparseAttention(nn.Module):
             raise ValueError(f"out must be a host [{B}, {T}, {D}] {x_host.dtype} tensor")
         compute = torch.cuda.current_stream(dev)
         h2d, d2h = self._copy_streams(dev)
+        self._issue_host(x_host, out, chunks, dev, compute, h2d, d2h, self._side_stream(dev))
+        d2h.synchronize()
+        return out
+
+    def _issue_host(self, x_host, out, chunks, dev, compute, h2d, d2h, side, keep=None,
+                    graphed=False):
+        """Queue ``forward_host``'s copies and kernels without waiting for them;
+        on return ``compute`` is ordered after the last copy out.  With ``keep``
+        (a list; CUDA-graph capture) the device buffers are appended to it
+        instead of being handed to the allocator's cross-stream tracking."""
+        B, T, D = x_host.shape
         h2d.wait_stream(compute)  # device buffers below come from the compute stream's pool
         adaptive = self.topk_selector.adaptive
         if B > 1 or adaptive:
@@ -596,15 +619,20 @@ class GatedSparseAttention(nn.Module):
                 with torch.cuda.stream(h2d):
                     x_dev[b0:b1].copy_(x_host[b0:b1], non_blocking=True)
                 compute.wait_stream(h2d)
-                y = self.forward(x_dev[b0:b1])
+                y = self._forward_impl(x_dev[b0:b1], side=side)
                 d2h.wait_stream(compute)
                 with torch.cuda.stream(d2h):
                     out[b0:b1].copy_(y, non_blocking=True)
-                y.record_stream(d2h)
-            compute.wait_stream(d2h)
-            d2h.synchronize()
-            return out
-        return self._forward_host_rows(x_host, out, chunks, dev, compute, h2d, d2h)
+                if keep is None:
+                    y.record_stream(d2h)
+                else:
+                    keep.append(y)
+            if keep is not None:
+                keep.append(x_dev)
+        else:
+            self._forward_host_rows(x_host, out, chunks, dev, compute, h2d, d2h, side, keep,
+                                    graphed)
+        compute.wait_stream(d2h)
 
     def _copy_streams(self, device: torch.device):
         key = ("copy", device)
@@ -614,7 +642,8 @@ class GatedSparseAttention(nn.Module):
             self._streams[key] = pair
         return pair
 
-    def _forward_host_rows(self, x_host, out, chunks, dev, compute, h2d, d2h):
+    def _forward_host_rows(self, x_host, out, chunks, dev, compute, h2d, d2h, side, keep,
+                           graphed):
         """B == 1: row blocks [r0, r1) in sequence order, keys [0, r1) for each.
 
         Two compute streams: the side stream prepares block c (projection GEMM,
@@ -625,7 +654,7 @@ class GatedSparseAttention(nn.Module):
         block c's attention leaves idle."""
         _, T, D = x_host.shape
         H = self.num_heads
-        bounds = host_row_block_bounds(T, chunks)
+        bounds = host_row_block_bounds(T, chunks, graphed)
         # the copies in go first: everything else waits on them
         x_dev = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
         done_in = []
@@ -650,7 +679,8 @@ class GatedSparseAttention(nn.Module):
                    else None)
         bm_offs = [sum(bm_sizes[:i]) for i in range(len(bm_sizes))]
         parts_all = self.split(proj)
-        side = self._side_stream(dev)
+        if keep is not None:
+            keep.extend([x_dev, proj, q, k, v, attn, y, bm_flat])
         side.wait_stream(compute)  # the buffers above come from the current stream's pool
         blocks = list(zip(bounds[:-1], bounds[1:]))
 
@@ -683,7 +713,10 @@ class GatedSparseAttention(nn.Module):
             compute.wait_event(e)
             if isinstance(sel, tuple):
                 for t in sel:
-                    t.record_stream(compute)
+                    if keep is None:
+                        t.record_stream(compute)
+                    else:
+                        keep.append(t)
             if torch.is_tensor(sel):
                 with _Stage(self, "k:masked_attention", "gsa_b200/sparse_attn"):
                     ops.masked_attention(q[:, r0:r1], k[:, :r1], v[:, :r1], sel, self.scale, H,
@@ -697,10 +730,8 @@ class GatedSparseAttention(nn.Module):
             with torch.cuda.stream(d2h):
                 out[:, r0:r1].copy_(y[:, r0:r1], non_blocking=True)
         compute.wait_stream(side)
-        y.record_stream(d2h)
-        compute.wait_stream(d2h)
-        d2h.synchronize()
-        return out
+        if keep is None:
+            y.record_stream(d2h)
 
 
 # ── CUDA-graph replay ──────────────────────────────────────────────────────
@@ -757,4 +788,62 @@ class GraphedForward:
                                    f"got {tuple(x.shape)} {x.dtype}")
             self.x.copy_(x, non_blocking=True)
         self.graph.replay()
+        return self.out
+
+
+class GraphedForwardHost:
+    """``module.forward_host`` for one input shape, captured once as a CUDA graph.
+
+    The graph holds the whole host-to-host pipeline: the pinned copies in, the
+    row-block (or batch-group) computation on its two streams and the pinned
+    copies out.  Its buffers are pinned host tensors of its own: write the
+    activations into ``x`` (or pass them to the call, which copies them there on
+    the host), and read the result from ``out`` once the call returns; the next
+    call overwrites it.  A replay issues the pipeline as one graph launch, so the
+    GPU no longer waits for Python to issue each block's kernels while the
+    first blocks' inputs arrive.  Captured by address, as ``GraphedForward``.
+    """
+
+    def __init__(self, module: "GatedSparseAttention", shape, dtype: torch.dtype,
+                 device=None, chunks: Optional[int] = None, warmup: int = 2):
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("GraphedForwardHost needs a CUDA device")
+        if module._stage_events is not None:
+            raise RuntimeError("per-stage timing events cannot be captured; disable them first")
+        if dtype not in (torch.bfloat16, torch.float32):
+            raise RuntimeError(f"unsupported dtype {dtype}")
+        self.module, self.device = module, device
+        self.x = torch.zeros(tuple(shape), dtype=dtype).pin_memory()
+        self.out = torch.zeros(tuple(shape), dtype=dtype).pin_memory()
+        self._main = torch.cuda.Stream(device=device)
+        self._side = torch.cuda.Stream(device=device, priority=-1)
+        self._h2d = torch.cuda.Stream(device=device)
+        self._d2h = torch.cuda.Stream(device=device)
+        streams = (self._main, self._h2d, self._d2h, self._side)
+        self._main.wait_stream(torch.cuda.current_stream(device))
+        with torch.no_grad(), torch.cuda.stream(self._main):
+            for _ in range(max(1, warmup)):
+                module._issue_host(self.x, self.out, chunks, device, *streams, graphed=True)
+        self._main.synchronize()
+        self._keep: list = []
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph, stream=self._main):
+            module._issue_host(self.x, self.out, chunks, device, *streams, keep=self._keep,
+                               graphed=True)
+        self._held = (module._fused_weight, module._fused_bias,
+                      getattr(module.indexer, "_bias32", None),
+                      getattr(module.rotary_emb, "_tables", None), dict(module._workspaces))
+
+    def __call__(self, x_host: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x_host is not None:
+            if x_host.shape != self.x.shape or x_host.dtype != self.x.dtype or x_host.is_cuda:
+                raise RuntimeError(f"captured for a host {tuple(self.x.shape)} {self.x.dtype} "
+                                   f"tensor, got {tuple(x_host.shape)} {x_host.dtype} "
+                                   f"on {x_host.device}")
+            self.x.copy_(x_host)
+        stream = torch.cuda.current_stream(self.device)
+        self.graph.replay()
+        stream.synchronize()
         return self.out

@@ -60,3 +60,25 @@ def test_replay_on_another_stream_and_shape_check():
     assert torch.equal(out, ref)
     with pytest.raises(RuntimeError, match="captured for"):
         g(x[:, :-1])
+
+
+@pytest.mark.parametrize("name,chunks", [("tiny_bf16", 2), ("tiny_fp32", 2), ("cfg2", 4),
+                                         ("cfg2", None)])
+def test_host_replay_equals_forward_host(name, chunks):
+    """The captured host-to-host pipeline (pinned copies in, row blocks or batch
+    groups on two streams, pinned copies out) equals forward_host bit for bit."""
+    from gsa_gdn_benchmarkstudy_b200.workloads import CONFIGS
+    cfg = TEST_CONFIGS.get(name) or CONFIGS[name]
+    m = _model(cfg)
+    x0 = make_input(cfg)
+    x1 = torch.randn(x0.shape, generator=torch.Generator().manual_seed(3)).to(x0.dtype)
+    ref0 = m.forward_host(x0, chunks=chunks).clone()
+    ref1 = m.forward_host(x1, chunks=chunks).clone()
+    g = m.graphed_host(x0.shape, chunks=chunks)
+    out = g(x0)
+    assert out is g.out and not out.is_cuda and torch.equal(out, ref0)
+    assert torch.equal(g(x1), ref1)
+    g.x.copy_(x0)
+    assert torch.equal(g(), ref0)
+    with pytest.raises(RuntimeError, match="captured for"):
+        g(x0.cuda())

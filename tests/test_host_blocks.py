@@ -21,3 +21,14 @@ def test_default_counts_and_half_size_ends():
     assert len(host_row_block_bounds(4096)) - 1 == 2    # at least 2048 rows per block
     assert len(host_row_block_bounds(1024)) - 1 == 1
     assert len(host_row_block_bounds(4096, 4)) - 1 == 4  # an explicit count is honoured
+
+
+def test_graphed_default_counts():
+    """Replayed from a CUDA graph: up to 9 blocks, one per 1024 rows."""
+    b = host_row_block_bounds(16384, graphed=True)
+    sizes = [e - s for s, e in zip(b[:-1], b[1:])]
+    assert len(sizes) == 9 and sizes[0] == sizes[-1] == 1024 and set(sizes[1:-1]) == {2048}
+    assert len(host_row_block_bounds(4096, graphed=True)) - 1 == 4
+    assert len(host_row_block_bounds(65536, graphed=True)) - 1 == 9
+    assert len(host_row_block_bounds(1500, graphed=True)) - 1 == 1
+    assert host_row_block_bounds(4096, 2, graphed=True) == host_row_block_bounds(4096, 2)
