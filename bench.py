@@ -262,10 +262,13 @@ def run_ours(args, cfg, rank: int, world: int, device):
     model._stage_events = []
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(device.index if device.index is not None else 0) as clocks:
+        # the barrier comes after every rank's sampler has started: the samplers
+        # start at different times, and a rank that entered the timed loop early
+        # would count its wait for the others' first collective as step time
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record(stream)
