@@ -62,14 +62,15 @@ def test_replay_on_another_stream_and_shape_check():
         g(x[:, :-1])
 
 
-@pytest.mark.parametrize("name,chunks", [("tiny_bf16", 2), ("tiny_fp32", 2), ("cfg2", 4),
-                                         ("cfg2", None)])
-def test_host_replay_equals_forward_host(name, chunks):
+@pytest.mark.parametrize("name,chunks,adaptive", [
+    ("tiny_bf16", 2, False), ("tiny_fp32", 2, False), ("cfg2", 4, False), ("cfg2", None, False),
+    ("small_bf16", None, True)])
+def test_host_replay_equals_forward_host(name, chunks, adaptive):
     """The captured host-to-host pipeline (pinned copies in, row blocks or batch
     groups on two streams, pinned copies out) equals forward_host bit for bit."""
     from gsa_gdn_benchmarkstudy_b200.workloads import CONFIGS
     cfg = TEST_CONFIGS.get(name) or CONFIGS[name]
-    m = _model(cfg)
+    m = _model(cfg, adaptive)
     x0 = make_input(cfg)
     x1 = torch.randn(x0.shape, generator=torch.Generator().manual_seed(3)).to(x0.dtype)
     ref0 = m.forward_host(x0, chunks=chunks).clone()

@@ -70,6 +70,8 @@ def test_graphed_forward_refuses_cpu_device():
     m = GatedSparseAttention(**cfg.module_kwargs())
     with pytest.raises(RuntimeError, match="CUDA"):
         m.graphed((cfg.B, cfg.T, cfg.D), device="cpu")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m.graphed_host((cfg.B, cfg.T, cfg.D), device="cpu")
 
 
 def test_fused_projection_layout():
