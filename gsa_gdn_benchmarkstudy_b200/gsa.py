@@ -798,8 +798,9 @@ class GraphedForwardHost:
     row-block (or batch-group) computation on its two streams and the pinned
     copies out.  Its buffers are pinned host tensors of its own: write the
     activations into ``x`` (or pass them to the call, which copies them there on
-    the host), and read the result from ``out`` once the call returns; the next
-    call overwrites it.  A replay issues the pipeline as one graph launch, so the
+    the host: a CPU memcpy of the whole input, which a producer that writes into
+    ``x`` directly avoids), and read the result from ``out`` once the call
+    returns; the next call overwrites it.  A replay issues the pipeline as one graph launch, so the
     GPU no longer waits for Python to issue each block's kernels while the
     first blocks' inputs arrive.  Captured by address, as ``GraphedForward``.
     """
