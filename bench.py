@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--cpu-sample-rows", type=int, default=256)
     ap.add_argument("--adaptive-k", action="store_true",
                     help="opt-in variance-based k per row (not the reference module's fixed k)")
+    ap.add_argument("--profile-window", action="store_true",
+                    help="cudaProfilerStart/Stop around the timed device-resident steps, for "
+                         "ncu --profile-from-start off (the reference's capture windows)")
     return ap.parse_args()
 
 
@@ -269,12 +272,16 @@ def run_ours(args, cfg, rank: int, world: int, device):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        if args.profile_window:
+            torch.cuda.profiler.start()
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record(stream)
             step()
             ev[i][1].record(stream)
         torch.cuda.synchronize()
+        if args.profile_window:
+            torch.cuda.profiler.stop()
     if world > 1:
         dist.barrier()
     step_ms = [a.elapsed_time(b) for a, b in ev]
