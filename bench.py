@@ -6,8 +6,8 @@ One step = one forward of the configuration's whole batch (default cfg3:
 B=1, T=16384, D=2048, H=16, k=2048, bf16) on synthetic seeded inputs and
 weights.  For N > 1 the driver launches one rank per GPU under torchrun; B=1
 configurations shard query rows zig-zag over the ranks (k_I, K and V are
-all-gathered with NCCL; each rank keeps its own output rows), batched ones shard
-sequences.
+all-gathered with NCCL, and the output rows at the end, so every rank holds the
+whole output), batched ones shard sequences (outputs all-gathered likewise).
 
 Rank 0 prints ONE JSON line.  ``value`` is whole-job tokens/s with inputs
 resident in HBM, timed per step with CUDA events (max over ranks), L2 flushed
@@ -19,8 +19,15 @@ timed live with events on its launch stream; ``cpu_baseline`` times the CPU
 oracle (a restatement of gsa_ref.py) on a bounded row sample on this host.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle port of
-gsa_ref.py; the reference itself is Python and does not travel) on all host
-cores for the same workload and prints the same JSON line with impl=reference.
+gsa_ref.py) on all host cores for the same workload and prints the same JSON
+line with impl=reference; like ``cpu_baseline`` it times a row sample and
+extrapolates, and says so.
+
+``--gpu-reference`` (single GPU) adds ``gpu_reference``: the reference's own
+GPU module, gsa_triton/gsa_opt.py (Triton), unmodified and loaded from the
+reference checkout installed under baseline/_ref, timed with the reference
+harness's protocol (5 warm-up + 10 timed forwards, CUDA events) at cfg2 and at
+the bench's configuration.
 """
 from __future__ import annotations
 
@@ -42,13 +49,17 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "GSA fwd tokens/s at D=2048,T=16K (1-8 B200); indexer TFLOP/s, sparse-attn GB/s"
 UNIT = "tokens/s"
-# dram__bytes_read.sum + dram__bytes_write.sum of one masked-attention launch of
-# this bench at N=1, per config, from the ncu capture summarised in
-# profiles/masked_attn_cfg3_dram.md (306.33 MB read + 56.79 MB written).
+# dram__bytes_read.sum + dram__bytes_write.sum of one masked-attention launch at
+# N=1, per configuration, each from an ncu capture of that configuration's
+# bench command (the algorithmic bytes of a launch, for comparison: q, k, v, og
+# and out read/written once plus the bitmask, B*T*(5*D*2 + 4*ceil(T/128)*4)).
 ATTN_TRAFFIC_BYTES_PER_LAUNCH = {"cfg3": 363_120_000}
-ATTN_TRAFFIC_NOTE = ("ncu capture of one launch at N=1 (profiles/masked_attn_cfg3_dram.md); "
-                     "algorithmic bytes per launch: q, k, v, og, out 64 MiB each + bitmask 32 MiB "
-                     "= 369 MB")
+
+
+def workload_string(cfg) -> str:
+    """The workload name both arms print (the driver compares them)."""
+    return (f"{cfg.name}: B={cfg.B} T={cfg.T} D={cfg.D} H={cfg.H} d={cfg.d_head} "
+            f"H_I={cfg.n_idx_heads} d_I={cfg.d_indexer} k={cfg.k_eff}")
 
 
 def parse_args():
@@ -62,6 +73,8 @@ def parse_args():
     ap.add_argument("--cpu-sample-rows", type=int, default=256)
     ap.add_argument("--adaptive-k", action="store_true",
                     help="opt-in variance-based k per row (not the reference module's fixed k)")
+    ap.add_argument("--gpu-reference", action="store_true",
+                    help="also time the reference's Triton module (gsa_opt.py) from baseline/_ref")
     ap.add_argument("--profile-window", action="store_true",
                     help="cudaProfilerStart/Stop around the timed device-resident steps, for "
                          "ncu --profile-from-start off (the reference's capture windows)")
@@ -154,65 +167,155 @@ class ClockSampler:
 
 
 # ─────────────────────────────────────────────────────────────── CPU baseline
-def cpu_baseline(cfg, sample_rows: int, threads: int) -> dict:
-    """Time the CPU oracle (restated gsa_ref.py) on a bounded row sample.
+class CpuSample:
+    """The CPU oracle (restated gsa_ref.py) on a bounded row sample of a workload.
 
     Work shared by all rows (key/value/indexer-key projections + key RoPE over
-    the full sequence) is timed once; the per-row work is timed on
-    ``sample_rows`` query rows spread uniformly over T and scaled by T/S."""
-    from gsa_gdn_benchmarkstudy_b200.gsa import GatedSparseAttention
-    from gsa_gdn_benchmarkstudy_b200.workloads import init_weights_, make_input
-    from oracle import gsa_oracle as O
+    the full sequence) is timed whole; the per-row work is timed on
+    ``sample_rows`` query rows spread uniformly over T and scaled by T/rows
+    (and, for a batch, by B: its sequences cost the same).  The figure is an
+    extrapolation from the sample, and every line that carries it says so."""
 
-    torch.set_num_threads(threads)
-    m = GatedSparseAttention(**cfg.module_kwargs())
-    init_weights_(m, seed=1)
-    sd = m.to(cfg.torch_dtype).state_dict()
-    x = make_input(cfg)
-    total_s = 0.0
-    rows_desc = []
-    with torch.no_grad():
-        for b in range(cfg.B):
-            rows = O.spread_rows(cfg.T, sample_rows, offset=b)
-            tm: dict = {}
-            O.forward_rows(sd, x[b:b + 1], cfg.H, cfg.k_base, cfg.k_max, rows=rows,
-                           row_chunk=1, timings=tm)
-            total_s += tm["shared_s"] + tm["rows_s"] * cfg.T / len(rows)
-            rows_desc.append(len(rows))
-            if b == 0 and cfg.B > 1:
-                # sequences of a batch cost the same: extrapolate from the first
-                total_s *= cfg.B
-                break
-    return {"value": cfg.B * cfg.T / total_s, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": (f"{rows_desc[0]} query rows spread over T={cfg.T} of sequence 0 "
-                       f"(+ full-sequence key/value projections), per-row time scaled by "
-                       f"T/rows{' and by B' if cfg.B > 1 else ''}; oracle restatement of "
-                       f"gsa_ref.py in torch on the CPU, {cfg.dtype}")}
+    def __init__(self, cfg, sample_rows: int, threads: int):
+        from gsa_gdn_benchmarkstudy_b200.gsa import GatedSparseAttention
+        from gsa_gdn_benchmarkstudy_b200.workloads import init_weights_, make_input
+        from oracle import gsa_oracle as O
+
+        self.O, self.cfg, self.threads = O, cfg, threads
+        torch.set_num_threads(threads)
+        m = GatedSparseAttention(**cfg.module_kwargs())
+        init_weights_(m, seed=1)
+        self.sd = m.to(cfg.torch_dtype).state_dict()
+        self.x = make_input(cfg)[:1]
+        self.rows = O.spread_rows(cfg.T, sample_rows)
+
+    def seconds(self) -> float:
+        """Extrapolated CPU seconds of one whole forward, from one timed sample."""
+        cfg, tm = self.cfg, {}
+        with torch.no_grad():
+            self.O.forward_rows(self.sd, self.x, cfg.H, cfg.k_base, cfg.k_max, rows=self.rows,
+                                row_chunk=1, timings=tm)
+        return cfg.B * (tm["shared_s"] + tm["rows_s"] * cfg.T / len(self.rows))
+
+    def describe(self, value: float) -> dict:
+        cfg = self.cfg
+        return {"value": value, "unit": UNIT, "cores": self.threads, "kind": "port",
+                "extrapolated": True, "sample_rows": len(self.rows),
+                "sample": (f"{len(self.rows)} query rows spread over T={cfg.T} of sequence 0 "
+                           f"(+ full-sequence key/value projections), per-row time scaled by "
+                           f"T/rows{' and by B' if cfg.B > 1 else ''}: an extrapolation; "
+                           f"oracle restatement of gsa_ref.py in torch on the CPU, {cfg.dtype}")}
+
+
+def cpu_baseline(cfg, sample_rows: int, threads: int) -> dict:
+    s = CpuSample(cfg, sample_rows, threads)
+    return s.describe(cfg.B * cfg.T / s.seconds())
 
 
 # ─────────────────────────────────────────────────────────────── reference arm
 def run_reference(args, cfg, rank: int):
+    """The reference's CPU algorithm (oracle port of gsa_ref.py) on all host cores.
+    Each step is one row sample of the workload (the same sample size as our
+    line's cpu_baseline), extrapolated to the whole forward."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    vals = []
-    sample = max(8, min(args.cpu_sample_rows, 64))
+    sample = CpuSample(cfg, args.cpu_sample_rows, threads)
+    secs = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(cfg, sample, threads)
+        t = sample.seconds()
         if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.mean(vals)
+            secs.append(t)
+    ms = statistics.mean(secs) * 1e3
+    v = cfg.B * cfg.T / (ms / 1e3)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cfg.B * cfg.T / v * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": cfg.dtype, "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights)",
-        "config": {"workload": f"{cfg.name}: B={cfg.B} T={cfg.T} D={cfg.D} H={cfg.H} "
-                               f"k={cfg.k_eff}", "l2": "n/a (CPU)"},
-        "cpu_baseline": {**r, "value": v},
+        "dtype": "bf16" if cfg.dtype == "bf16" else "f32",
+        "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights; no dataset in the reference)",
+        "extrapolated": True,
+        "config": {"workload": workload_string(cfg), "global_batch": cfg.B, "seq_len": cfg.T,
+                   "l2": "n/a (CPU)"},
+        "cpu_baseline": sample.describe(v),
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ─────────────────────────────────────────────────────────────── reference GPU row
+def gpu_reference(cfg, device, names=("cfg2",)) -> dict:
+    """The reference's own GPU module, gsa_triton/gsa_opt.py (Triton kernels,
+    two streams), unmodified, loaded from the reference checkout installed under
+    baseline/_ref, and timed with the reference harness's protocol
+    (gsa_triton/benchmark.py:150-222: 5 warm-up + 10 timed forwards between two
+    CUDA events, tok/s = B*T/s) on the same seeded weights and inputs as our
+    arm.  Runs at each named configuration and at ``cfg``.
+
+    The stock module raises for T > 8192 on a GPU (its RotaryEmbedding rebuilds
+    the cos/sin cache from a CPU arange and the device's inv_freq,
+    gsa_opt.py:410-421); that error is recorded as the configuration's result.
+    A second entry then times the same module with its rotary cache built for
+    T on the host before the module moves to the GPU (the constructor's own
+    cache code, called with T; no reference code is changed), marked as such."""
+    from gsa_gdn_benchmarkstudy_b200 import GatedSparseAttention as Ours
+    from gsa_gdn_benchmarkstudy_b200.workloads import CONFIGS, init_weights_, make_input
+
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "gsa_opt.py").exists():
+        return {"unavailable": "baseline/_ref/gsa_opt.py not present (reference not installed)"}
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    try:
+        import gsa_opt  # noqa: F401  (the reference's own module)
+    except Exception as exc:  # triton or the module itself failed to import
+        return {"unavailable": f"import gsa_opt failed: {type(exc).__name__}: {exc}"[:300]}
+
+    def one(c, prebuild_rotary: bool) -> dict:
+        res = {"workload": workload_string(c), "impl": "gsa_triton/gsa_opt.py (unmodified)"}
+        model = x = None
+        try:
+            kw = c.module_kwargs()
+            ref = gsa_opt.GatedSparseAttention(**kw)
+            ours = init_weights_(Ours(**kw))
+            ref.load_state_dict(ours.state_dict(), strict=True)
+            if prebuild_rotary:
+                ref.rotary_emb._set_cos_sin_cache(c.T)
+                res["note"] = (f"rotary cos/sin cache built for T={c.T} on the host before .to(cuda) "
+                               "(the stock module raises for T > 8192 on a GPU)")
+            model = ref.to(device).to(c.torch_dtype).eval()
+            model.fuse_projections()
+            x = make_input(c, device=device)
+            with torch.no_grad():
+                for _ in range(5):
+                    model(x)
+                torch.cuda.synchronize(device)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(10):
+                    model(x)
+                e1.record()
+                torch.cuda.synchronize(device)
+            ms = e0.elapsed_time(e1) / 10
+            res.update({"ms_per_step": round(ms, 3), "value": round(c.B * c.T / (ms / 1e3), 1),
+                        "unit": UNIT})
+        except Exception as exc:
+            res["error"] = f"{type(exc).__name__}: {exc}"[:300]
+        finally:
+            del model, x
+            torch.cuda.synchronize(device)
+            torch.cuda.empty_cache()
+        return res
+
+    out = {"protocol": "gsa_triton/benchmark.py:150-222 (5 warm-up + 10 timed, CUDA events)",
+           "runs": []}
+    todo = [CONFIGS[n] for n in names if n != cfg.name] + [cfg]
+    for c in todo:
+        r = one(c, prebuild_rotary=False)
+        out["runs"].append(r)
+        if "error" in r and c.T > 8192:
+            out["runs"].append(one(c, prebuild_rotary=True))
+    return out
 
 
 # ─────────────────────────────────────────────────────────────── our arm
@@ -246,8 +349,9 @@ def run_ours(args, cfg, rank: int, world: int, device):
         runner = ShardedGSA(model, dist.group.WORLD, T=cfg.T, B=cfg.B)
         x_local_host = runner.local_input(x_host).pin_memory()
         x_dev = x_local_host.to(device)
-        # each rank keeps its own output rows: the job's output is their union
-        step = lambda: runner(x_dev, gather=False)  # noqa: E731
+        # the whole step: every rank ends with the full output (the output rows
+        # are all-gathered, as for the k_I / K / V rows before them)
+        step = lambda: runner(x_dev)  # noqa: E731
         e2e_step = lambda: runner.forward_host(x_local_host)  # noqa: E731
     else:
         x_dev = x_host.to(device)
@@ -303,6 +407,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
         if name.startswith("k:"):
             own_launches += n_launch
     stage_avg = {k: sum(v) / len(v) for k, v in stage_ms.items()}
+    stage_step = {k: sum(v) / args.steps for k, v in stage_ms.items()}
     split = time_indexer_and_topk(model, x_dev if world == 1 else None, cfg)
 
     # ---------------- end-to-end through the public API, host buffers
@@ -362,23 +467,28 @@ def run_ours(args, cfg, rank: int, world: int, device):
     if attn_ms:
         # algorithmic work of one launch: QK^T + PV over the causal key range of the
         # launch's rows (the formulation the kernel computes), B sequences / world ranks
-        flops = wm.attn_dense_flops / world / stage_count(stage_ms, "k:masked_attention", args.steps)
+        n_at = stage_count(stage_ms, "k:masked_attention", args.steps)
+        flops = wm.attn_dense_flops / world / n_at
         achieved = flops / (attn_ms / 1e3) / 1e12
         peak = pk["bf16_tflops"]
+        traffic = ATTN_TRAFFIC_BYTES_PER_LAUNCH.get(cfg.name) if world == 1 else None
         rl = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-              "frac": round(achieved / peak, 4),
-              "traffic": ATTN_TRAFFIC_BYTES_PER_LAUNCH.get(cfg.name) if world == 1 else None,
+              "frac": round(achieved / peak, 4), "traffic": traffic,
               "kernel": "masked_attn_kernel (tcgen05)", "peak_kind": f"bf16 burst, {pk['_source']}",
-              "ms_per_launch": round(attn_ms, 4)}
-        if rl["traffic"] is not None:
-            rl["traffic_note"] = ATTN_TRAFFIC_NOTE
+              "ms_per_launch": round(attn_ms, 4),
+              # the same launch time over the flops of the selected (query, key)
+              # pairs only: the share of the tensor work the selection needs
+              "useful_frac": round(wm.attn_sparse_flops / world / n_at / (attn_ms / 1e3) / 1e12
+                                   / peak, 4),
+              "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                 f"of this bench at {cfg.name}, N=1" if traffic is not None else
+                                 "no ncu capture of this configuration and N")}
     extra = {}
     if split:
         extra["indexer_ms"] = round(split["indexer"], 4)
         extra["topk_ms"] = round(split["topk"], 4)
         extra["indexer_tflops"] = round(wm.indexer_flops / (split["indexer"] / 1e3) / 1e12, 2)
     if attn_ms:
-        n_at = stage_count(stage_ms, "k:masked_attention", args.steps)
         extra["sparse_attn_gather_equiv_gbs"] = round(
             wm.attn_gather_bytes / world / n_at / (attn_ms / 1e3) / 1e9, 1)
     line = {
@@ -387,8 +497,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16"
         if cfg.dtype == "bf16" else "f32",
         "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights; no dataset in the reference)",
-        "config": {"workload": f"{cfg.name}: B={cfg.B} T={cfg.T} D={cfg.D} H={cfg.H} d=128 "
-                               f"H_I=4 d_I=64 k={cfg.k_eff}",
+        "config": {"workload": workload_string(cfg),
                    "global_batch": cfg.B, "seq_len": cfg.T,
                    "parallelism": ("single GPU" if world == 1 else
                                    ("query-row zig-zag shards" if cfg.B == 1 else "batch shards")),
@@ -403,12 +512,15 @@ def run_ours(args, cfg, rank: int, world: int, device):
                 **({"forward_host_ms_per_step": round(eager_host_ms, 4)}
                    if eager_host_ms is not None else {})},
         "roofline": rl,
-        "stage_ms": {(k[2:] if k.startswith("k:") else k.split(":", 1)[1] + " (cuBLAS)"): round(v, 4)
-                     for k, v in stage_avg.items()},
+        # per stage: device time summed over the stage's launches in one step
+        # (events on the stream that issues it; rank 0)
+        "stage_ms": {stage_label(k): round(v, 4) for k, v in stage_step.items()},
         **extra,
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_sample_rows, os.cpu_count() or 1)
+    if world == 1 and args.gpu_reference:
+        line["gpu_reference"] = gpu_reference(cfg, device)
     print(json.dumps(line), flush=True)
 
 
@@ -443,6 +555,12 @@ def time_indexer_and_topk(model, x, cfg, iters: int = 5):
         torch.cuda.synchronize()
         res[name] = e0.elapsed_time(e1) / iters
     return res
+
+
+def stage_label(name: str) -> str:
+    """Stage names of the bench line: our kernels bare, library calls tagged."""
+    kind, _, rest = name.partition(":")
+    return {"k": rest, "lib": f"{rest} (cuBLAS)", "comm": f"{rest} (NCCL)"}.get(kind, name)
 
 
 def stage_count(stage_ms: dict, name: str, steps: int) -> float:

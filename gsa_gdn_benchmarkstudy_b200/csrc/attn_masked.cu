@@ -457,18 +457,35 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 
 }  // namespace
 
+int masked_attention_regs(int* expected) {
+  *expected = kLaunchRegs;
+  static std::atomic<int> regs{0};
+  int r = regs.load(std::memory_order_acquire);
+  if (r == 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, masked_attn_kernel) != cudaSuccess) return -1;
+    r = fa.numRegs;
+    regs.store(r, std::memory_order_release);
+  }
+  return r;
+}
+
 cudaError_t launch_masked_attention(const CUtensorMap& qmap, const CUtensorMap& kmap,
                                     const CUtensorMap& vmap, const MaskedAttnArgs& a,
                                     cudaStream_t stream) {
   if (a.B == 0 || a.Tq == 0 || a.Tkv == 0) return cudaSuccess;
-  static bool attr_set[64] = {false};
+  // the setmaxnreg split is valid only for the register count it was written for
+  int expected = 0;
+  if (masked_attention_regs(&expected) != expected) return cudaErrorNotSupported;
+  // once per device; two threads racing here both set the same attribute
+  static std::atomic<bool> attr_set[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(masked_attn_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const int n_qt = (a.Tq + kAtBM - 1) / kAtBM;
   const int pairs = a.B * a.H;

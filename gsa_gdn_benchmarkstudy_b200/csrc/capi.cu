@@ -3,6 +3,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "kernels.h"
@@ -10,7 +11,7 @@
 namespace {
 
 constexpr int kVersion = 10000;  // 1.0.0
-constexpr int kMaxDevices = 64;
+using gsa::kMaxDevices;
 
 thread_local char g_last_error[256] = "";
 
@@ -21,7 +22,7 @@ __device__ int g_dev_err;
 // gsa_indexer_topk otherwise keeps in the caller's workspace.  Every GPU that
 // loads the library holds it until the process exits.  In host code this name
 // stands for the host-side shadow, not a device address: kernels receive the
-// address that noalloc_scratch() looks up per device.
+// address that device_state() looks up per device.
 static __device__ __align__(256) float g_noalloc_scratch[GSA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
 int set_cuda_error(cudaError_t e) {
@@ -35,11 +36,15 @@ int set_error(int code, const char* what) {
   return code;
 }
 
-// Per-device state: sm_100 check result and the address of g_dev_err.
+// Per-device state: sm_100 check result, the address of g_dev_err and the
+// address of g_noalloc_scratch.  Filled once per device under g_dev_mu; `ready`
+// is published with a release store after the other fields, so a thread that
+// reads it true with an acquire load (outside the mutex) sees them filled.
 struct DeviceState {
-  bool ready = false;
+  std::atomic<bool> ready{false};
   bool sm100 = false;
   int* err = nullptr;
+  float* noalloc = nullptr;
 };
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -50,48 +55,32 @@ int device_state(DeviceState** out) {
   if (e != cudaSuccess) return set_cuda_error(e);
   if (dev < 0 || dev >= kMaxDevices) return set_error(GSA_ERR_NO_DEVICE, "device index out of range");
   DeviceState& st = g_dev[dev];
-  if (!st.ready) {
+  if (!st.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    if (!st.ready) {
+    if (!st.ready.load(std::memory_order_relaxed)) {
       int major = 0;
       e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
       if (e != cudaSuccess) return set_cuda_error(e);
       st.sm100 = (major == 10);
       if (st.sm100) {
+        // Both lookups need the library's module loaded on this device, which
+        // only an sm_100 device can do (the library holds sm_100a code only).
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_dev_err);
         if (e != cudaSuccess) return set_cuda_error(e);
         st.err = static_cast<int*>(p);
+        // The address of the built-in scratch of gsa_indexer_topk_noalloc on
+        // this device (with this device current); the lookup allocates nothing.
+        p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        st.noalloc = static_cast<float*>(p);
       }
-      st.ready = true;
+      st.ready.store(true, std::memory_order_release);
     }
   }
   if (!st.sm100) return set_error(GSA_ERR_NO_DEVICE, "current device is not sm_100 (B200)");
   *out = &st;
-  return GSA_OK;
-}
-
-// Device address of g_noalloc_scratch on the current device.  Looked up once
-// per device (with that device current) on the first gsa_indexer_topk_noalloc
-// call there; the lookup allocates nothing.
-float* g_noalloc_ptr[kMaxDevices] = {nullptr};
-std::mutex g_noalloc_mu;
-
-int noalloc_scratch(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_cuda_error(e);
-  if (dev < 0 || dev >= kMaxDevices) return set_error(GSA_ERR_NO_DEVICE, "device index out of range");
-  if (!g_noalloc_ptr[dev]) {
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      float* p = nullptr;
-      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch);
-      if (e != cudaSuccess) return set_cuda_error(e);
-      g_noalloc_ptr[dev] = p;
-    }
-  }
-  *out = g_noalloc_ptr[dev];
   return GSA_OK;
 }
 
@@ -350,11 +339,11 @@ int gsa_indexer_topk_noalloc(const void* q, int64_t q_stride, const void* k, int
   }
   if (bitmask && bitmask_words < gsa_bitmask_words(Tkv))
     return set_error(GSA_ERR_INVALID_ARG, "bitmask_words < gsa_bitmask_words(Tkv)");
-  float* scratch = nullptr;
-  int rc = noalloc_scratch(&scratch);
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);  // GSA_ERR_NO_DEVICE on anything but sm_100
   if (rc) return rc;
   return indexer_topk_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
-                           q_pos0, H_I, d_I, k_sel, scratch, indices, mask, bitmask,
+                           q_pos0, H_I, d_I, k_sel, st->noalloc, indices, mask, bitmask,
                            bitmask_words, static_cast<cudaStream_t>(stream));
 }
 
@@ -527,6 +516,15 @@ int gsa_masked_attention(const void* q, int64_t q_stride, const void* k, int64_t
   a.q_pos0 = q_pos0;
   a.H = H;
   a.err = st->err;
+  int expected = 0;
+  const int regs = gsa::masked_attention_regs(&expected);
+  if (regs != expected) {
+    std::snprintf(g_last_error, sizeof(g_last_error),
+                  "masked_attn_kernel was built with %d registers per thread; its setmaxnreg "
+                  "split needs %d",
+                  regs, expected);
+    return GSA_ERR_UNSUPPORTED;
+  }
   return finish(gsa::launch_masked_attention(qmap, kmap, vmap, a, static_cast<cudaStream_t>(stream)));
 }
 

@@ -257,17 +257,6 @@ __device__ __forceinline__ float fast_tanh(float x) {
   return y;
 }
 
-__device__ __forceinline__ float fast_rcp(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// Logistic function 1 / (1 + e^-x) evaluated as 1 / (1 + 2^(-x * log2 e)).
-__device__ __forceinline__ float sigmoid_fast(float x) {
-  return fast_rcp(1.0f + fast_ex2(-1.4426950408889634f * x));
-}
-
 // Logistic function through expf, for element-wise gates where the result is
 // rounded to the module dtype.
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
@@ -290,35 +279,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-// max of packed bf16 pairs
-__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// Packed logistic function for two lanes: 1 / (1 + 2^y) with y = -x*log2(e)
-// given as `y2`.  2^y runs on the MUFU (ex2.approx); the reciprocal runs on
-// the FMA pipe: a bit-level seed r0 = bits^-1(C - bits(d)) for 1/d (the
-// classic integer-subtraction seed for reciprocals; C = 0x7EF311C2 minimises
-// the seed's relative error over a binade, 5%) refined by three Newton-Raphson
-// steps r <- r + r*(1 - d*r) to ~6e-8 relative error.  y is clamped at 60 so
-// d stays finite (the logistic of such arguments is below 1e-18).
-__device__ __forceinline__ uint64_t sigmoid2_nr(uint64_t y2) {
-  const float e0 = fast_ex2(fminf(f2_lo(y2), 60.f));
-  const float e1 = fast_ex2(fminf(f2_hi(y2), 60.f));
-  const uint64_t m1 = f2_pack(-1.f, -1.f);
-  const uint64_t nd = f2_fma(f2_pack(e0, e1), m1, m1);  // -(1 + 2^y)
-  // seed for 1/d from the bits of -d: (C + 2^31) - bits(-d) == C - bits(d)
-  constexpr uint32_t kSeed = 0x7EF311C2u + 0x80000000u;
-  uint64_t r = (static_cast<uint64_t>(kSeed - static_cast<uint32_t>(nd >> 32)) << 32) |
-               (kSeed - static_cast<uint32_t>(nd));
-  const uint64_t one = f2_pack(1.f, 1.f);
-#pragma unroll
-  for (int it = 0; it < 3; ++it) r = f2_fma(r, f2_fma(nd, r, one), r);
-  return r;
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

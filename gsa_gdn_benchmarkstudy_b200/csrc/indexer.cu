@@ -337,14 +337,15 @@ __global__ void fill_upper_kernel(float* out, int64_t out_stride, int Tq, int Tk
 cudaError_t launch_indexer_tc(const CUtensorMap& qmap, const CUtensorMap& kmap,
                               const IndexerArgs& a, cudaStream_t stream) {
   if (a.B == 0 || a.Tq == 0 || a.Tkv == 0) return cudaSuccess;
-  static bool attr_set[64] = {false};
+  // once per device; two threads racing here both set the same attribute
+  static std::atomic<bool> attr_set[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(indexer_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kIdxSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const int n_qt = (a.Tq + kIdxBM - 1) / kIdxBM;
   const int max_key = min(a.q_pos0 + a.Tq, a.Tkv);

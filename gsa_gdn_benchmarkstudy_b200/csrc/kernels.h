@@ -2,9 +2,14 @@
 // Argument checking happens in capi.cu; these assume valid arguments.
 #pragma once
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace gsa {
+
+// Devices the per-device launch state covers (cudaGetDevice indices).
+constexpr int kMaxDevices = 64;
 
 cudaError_t launch_rope_gates(const void* q_src, const void* k_src, const void* v_src,
                               const void* vg_src, int64_t src_stride, int dtype, int B, int T,
@@ -77,6 +82,12 @@ struct MaskedAttnArgs {
   int B, Tq, Tkv, q_pos0, H;
   int* err;
 };
+// Registers per thread that the build gave masked_attn_kernel
+// (cudaFuncGetAttributes), and in *expected the count its setmaxnreg split is
+// written for.  launch_masked_attention refuses (cudaErrorNotSupported) to
+// launch a build where the two differ: a split larger than the launch's
+// allocation would wait for registers forever.
+int masked_attention_regs(int* expected);
 cudaError_t launch_masked_attention(const CUtensorMap& qmap, const CUtensorMap& kmap,
                                     const CUtensorMap& vmap, const MaskedAttnArgs& a,
                                     cudaStream_t stream);

@@ -24,6 +24,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import ops
+from .gsa import _Stage
 
 Block = Tuple[int, int]
 
@@ -174,16 +175,23 @@ class ShardedGSA:
                                              var_rows=self.B * self.T)
             else:
                 y = self.model(x_local)
-            return gather_batch(y, self.group) if gather else y
+            if not gather:
+                return y
+            with _Stage(self.model, "comm:out_allgather", "gsa_b200/out_allgather"):
+                return gather_batch(y, self.group)
         return self._forward_rows(x_local, gather)
 
     def _forward_rows(self, x_loc: torch.Tensor, gather: bool = True) -> torch.Tensor:
         m = self.model
-        proj = m.project(x_loc)
+        with _Stage(m, "lib:proj_gemm", "gsa_b200/fused_proj"):
+            proj = m.project(x_loc)
         outs = self._rows_from_projection(proj, x_loc.dtype)
-        out_local = F.linear(torch.cat(outs, dim=1), m.o_proj.weight)
-        return (gather_rows(out_local, self.T, self.group, self._row_order(x_loc.device))
-                if gather else out_local)
+        with _Stage(m, "lib:o_proj", "gsa_b200/o_proj"):
+            out_local = F.linear(torch.cat(outs, dim=1), m.o_proj.weight)
+        if not gather:
+            return out_local
+        with _Stage(m, "comm:out_allgather", "gsa_b200/out_allgather"):
+            return gather_rows(out_local, self.T, self.group, self._row_order(x_loc.device))
 
     def _rows_from_projection(self, proj: torch.Tensor, dtype, per_block=None) -> list:
         """Everything after the projection GEMM of this rank's rows: gathers,
@@ -197,12 +205,14 @@ class ShardedGSA:
         order = self._row_order(dev)
         parts = m.split(proj)
         # the selection needs only the indexer keys of the whole sequence (2 MB at T=16K)
-        ik_full = gather_rows(parts["ik"].contiguous(), T, self.group, order)
+        with _Stage(m, "comm:ik_allgather", "gsa_b200/ik_allgather"):
+            ik_full = gather_rows(parts["ik"].contiguous(), T, self.group, order)
         cos, sin = m.rotary_emb(T, dev, dtype)
         pos = self._positions(dev)
-        q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
-                                 sin.index_select(0, pos), H, v_src=parts["v"],
-                                 vg_src=parts["vg"])
+        with _Stage(m, "k:rope_gates", "gsa_b200/rope_gates"):
+            q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
+                                     sin.index_select(0, pos), H, v_src=parts["v"],
+                                     vg_src=parts["vg"])
         # keys and values of the whole sequence: gathered while the blocks select
         gk = torch.empty((self.world, *k.shape[1:]), dtype=k.dtype, device=dev)
         gv = torch.empty_like(gk)
@@ -228,10 +238,12 @@ class ShardedGSA:
             bms = self._block_bitmasks(dev)
             sels = [m.select_rows(pb, ik_full[:, :e], s, tkv=e, bitmask_out=bm)
                     for (pb, s, e, _, _), bm in zip(blocks, bms)]
-        wk.wait()
-        wv.wait()
-        k_full = unshard_rows(gk, order)
-        v_full = unshard_rows(gv, order)
+        # the part of the K/V all-gathers that the selection did not hide
+        with _Stage(m, "comm:kv_allgather_wait", "gsa_b200/kv_allgather_wait"):
+            wk.wait()
+            wv.wait()
+            k_full = unshard_rows(gk, order)
+            v_full = unshard_rows(gv, order)
         outs = []
         for i, ((pb, s, e, o, n), sel) in enumerate(zip(blocks, sels)):
             a = m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e], q[:, o:o + n], q_pos0=s)

@@ -247,9 +247,10 @@ GSA_API int gsa_indexer_topk(const void* q, int64_t q_stride,
  *     bytes (B * Tq rows of round-up-to-4(Tkv) floats; e.g. one 2048-token
  *     sequence).  Larger calls return GSA_ERR_UNSUPPORTED and say so in
  *     gsa_last_error_string(); use gsa_indexer_topk with a workspace then.
- *   - First call on a device: it looks up the device address of the buffer,
+ *   - First call on a device: the first call of any gsa_* entry point on a
+ *     device (this one included) looks up the device address of the buffer,
  *     once per device, with that device current.  Make that first call before
- *     any stream capture.
+ *     any stream capture.  A device other than sm_100 gets GSA_ERR_NO_DEVICE.
  *   - Shared state: every call on a device uses the same buffer, which keeps
  *     the scores of the last call.  Nothing in it needs to start at zero,
  *     because each call writes every score it reads.  Calls whose work

@@ -1,7 +1,8 @@
 """Whole-forward parity of GatedSparseAttention on the GPU against the reference.
 
 Golden outputs come from running gsa_triton/gsa_ref.py itself (tests/golden);
-larger sequence lengths are checked row-by-row against the pinned CPU oracle.
+larger sequence lengths are checked row-by-row against the pinned CPU oracle
+(cfg3, cfg4 and cfg5 in test_gpu_configs.py).
 Tolerance (bf16): output within 2e-2 max-abs (the contract) and within 3e-2
 relative Frobenius error.  fp32: 1e-4 relative on 99% of rows (a row may differ
 more only where an exact-tie selection flipped) and 2e-2 max-abs everywhere."""
@@ -70,19 +71,6 @@ def test_forward_cfg2_rows_vs_reference():
     cfg = CONFIGS["cfg2"]
     out = make_model(cfg)(make_input(cfg).cuda())
     check_bf16(out[:, g["rows"]], g["out"])
-
-
-def test_forward_cfg3_rows_vs_oracle():
-    """T = 16384 (the headline config): sampled rows against the pinned oracle."""
-    cfg = CONFIGS["cfg3"]
-    x = make_input(cfg)
-    m = make_model(cfg)
-    out = m(x.cuda())
-    assert torch.isfinite(out).all()
-    rows = [0, 2047, 2048, 9000, 16383]
-    sd = {k: v.cpu() for k, v in m.state_dict().items()}
-    ref = O.forward_rows(sd, x, cfg.H, cfg.k_base, cfg.k_max, rows=rows, row_chunk=1)
-    check_bf16(out[:, rows], ref)
 
 
 @pytest.mark.parametrize("name", ["tiny_bf16", "tiny_fp32"])

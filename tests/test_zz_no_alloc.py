@@ -5,12 +5,21 @@ that owns all device memory, or a runtime that fixes its memory budget at
 start-up (an allocation can synchronise the device and fragment the pool).
 They cannot pass gsa_indexer_topk the scratch it takes as `workspace`, so
 this variant keeps that scratch in a buffer built into the library (16 MiB per
-GPU).  The test calls it through the C ABI and checks its outputs against
-gsa_indexer_topk with a caller workspace, on two calls in a row.  The second
-call uses other shapes, so it also shows that the scores the first call left
-in the shared buffer do not leak into the second.  It also checks that a call
-needing more scratch than the built-in buffer holds is refused with a clear
-message.
+GPU).  The test calls it through the C ABI and checks:
+
+* its outputs against gsa_indexer_topk with a caller workspace, on calls in a
+  row whose shapes differ, so the scores one call leaves in the shared buffer
+  must not leak into the next.  The caller workspace of the comparison call is
+  filled with a sentinel (1e30) first: a score column that the kernels read
+  without writing it would then be selected there and not here;
+* its selections against the CPU oracle's scores under the (score desc, index
+  asc) rule, modulo keys within 1e-4 (relative) of the k-th score (the
+  tensor-core scores are ~1e-5 from the oracle's);
+* the exact size limit: B=1, Tq=Tkv=2048 needs exactly the 16 MiB built in and
+  is accepted, a larger call is refused with a clear message;
+* that the calls take no device memory: the driver's free-memory figure
+  (cudaMemGetInfo) is the same before and after them (the first call, which
+  loads the library's kernels onto the device, comes before the measurement).
 
 The file name sorts last, so a run that stops at the first failure has run
 every other test before this one."""
@@ -19,19 +28,21 @@ import torch
 
 from gsa_gdn_benchmarkstudy_b200 import _lib
 from gsa_gdn_benchmarkstudy_b200.build import build
+from oracle import gsa_oracle as O
 
 pytestmark = pytest.mark.gpu
 torch.set_grad_enabled(False)
 
 GSA_ERR_UNSUPPORTED = 3
+SCRATCH_BYTES = 16 << 20
 
 
 def _inputs(B, Tq, Tkv, seed):
     g = torch.Generator().manual_seed(seed)
-    q = (torch.randn(B, Tq, 4 * 64, generator=g) * 0.9).bfloat16().cuda()
-    k = (torch.randn(B, Tkv, 64, generator=g) * 0.9).bfloat16().cuda()
-    w = torch.randn(B, Tq, 4, generator=g).bfloat16().cuda()
-    bias = (torch.randn(4, generator=g) * 0.1).float().cuda()
+    q = (torch.randn(B, Tq, 4 * 64, generator=g) * 0.9).bfloat16()
+    k = (torch.randn(B, Tkv, 64, generator=g) * 0.9).bfloat16()
+    w = torch.randn(B, Tq, 4, generator=g).bfloat16()
+    bias = (torch.randn(4, generator=g) * 0.1).float()
     return q, k, w, bias
 
 
@@ -41,10 +52,11 @@ def _outputs(B, Tq, k_sel, words):
             torch.full((B, Tq, words), -1, dtype=torch.int32, device="cuda"))
 
 
-def _run(lib, noalloc, q, k, w, bias, Tkv, q_pos0, k_sel):
+def _call(lib, noalloc, dev_in, Tkv, q_pos0, k_sel, outs):
+    q, k, w, bias = dev_in
     B, Tq = q.shape[0], q.shape[1]
-    words = lib.gsa_bitmask_words(Tkv)
-    idx, msk, bm = _outputs(B, Tq, k_sel, words)
+    idx, msk, bm = outs
+    words = bm.shape[-1]
     stream = torch.cuda.current_stream().cuda_stream
     common = (q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), w.data_ptr(), w.stride(1),
               bias.data_ptr(), 0.125, 0, B, Tq, Tkv, q_pos0, 4, 64, k_sel)
@@ -53,39 +65,85 @@ def _run(lib, noalloc, q, k, w, bias, Tkv, q_pos0, k_sel):
                                           bm.data_ptr(), words, stream)
     else:
         need = lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv)
-        ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+        ws = torch.empty(need // 4, dtype=torch.float32, device="cuda").fill_(1e30)
         rc = lib.gsa_indexer_topk(*common, ws.data_ptr(), need, idx.data_ptr(), msk.data_ptr(),
                                   bm.data_ptr(), words, stream)
     assert rc == 0, lib.gsa_last_error_string().decode()
-    torch.cuda.synchronize()
-    return idx.cpu(), msk.cpu(), bm.cpu()
 
 
-def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row():
+def _check_vs_oracle(cpu_in, Tkv, q_pos0, k_sel, idx, msk):
+    q, k, w, bias = cpu_in
+    B, Tq = q.shape[0], q.shape[1]
+    ref = O.indexer_scores(q.view(B, Tq, 4, 64), k, w, bias, 0.125,
+                           q_pos=torch.arange(q_pos0, q_pos0 + Tq))
+    ridx, rmsk = O.topk_select_stable(ref, k_sel)
+    for b in range(B):
+        for r in range(Tq):
+            a = set(idx[b, r][msk[b, r].bool()].tolist())
+            c = set(ridx[b, r][rmsk[b, r]].tolist())
+            assert len(a) == len(c) == min(q_pos0 + r + 1, Tkv, k_sel)
+            if a == c:
+                continue
+            kth = ref[b, r, list(c)].min().item()
+            for j in a.symmetric_difference(c):
+                assert abs(ref[b, r, j].item() - kth) <= 1e-4 * abs(kth), (b, r, j)
+
+
+CASES = [  # B, Tq, Tkv, q_pos0, k_sel, seed
+    (1, 700, 1500, 800, 256, 11),
+    (2, 160, 160, 0, 48, 12),
+    (1, 2048, 2048, 0, 256, 14),  # exactly the 16 MiB built in
+]
+
+
+def test_noalloc_matches_workspace_entry_and_oracle_on_calls_in_a_row():
     build()
     lib = _lib.load()
-    cases = [(1, 700, 1500, 800, 256, 11), (2, 160, 160, 0, 48, 12)]
-    for B, Tq, Tkv, q_pos0, k_sel, seed in cases:
-        q, k, w, bias = _inputs(B, Tq, Tkv, seed)
-        got = _run(lib, True, q, k, w, bias, Tkv, q_pos0, k_sel)
-        ref = _run(lib, False, q, k, w, bias, Tkv, q_pos0, k_sel)
-        # same kernels on the same inputs: identical indices, mask and bitmask
-        for a, b in zip(got, ref):
-            assert torch.equal(a, b)
+    assert lib.gsa_indexer_topk_workspace_size(1, 2048, 2048) == SCRATCH_BYTES
+    prepared = []
+    for B, Tq, Tkv, q_pos0, k_sel, seed in CASES:
+        cpu_in = _inputs(B, Tq, Tkv, seed)
+        dev_in = tuple(t.cuda() for t in cpu_in)
+        words = lib.gsa_bitmask_words(Tkv)
+        prepared.append((cpu_in, dev_in, Tkv, q_pos0, k_sel,
+                         _outputs(B, Tq, k_sel, words), _outputs(B, Tq, k_sel, words)))
+    # the first call on this device loads the library's kernels; then every
+    # input and output exists, and the no-allocation calls must leave the
+    # device's free memory as it is
+    cpu_in, dev_in, Tkv, q_pos0, k_sel, got, _ = prepared[0]
+    _call(lib, True, dev_in, Tkv, q_pos0, k_sel, got)
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for _, dev_in, Tkv, q_pos0, k_sel, got, _ in prepared + prepared[:1]:
+        _call(lib, True, dev_in, Tkv, q_pos0, k_sel, got)
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free_before
+    # each no-allocation call against the workspace entry point on the same
+    # inputs, calls in a row with different shapes
+    for cpu_in, dev_in, Tkv, q_pos0, k_sel, got, ref in prepared:
+        _call(lib, True, dev_in, Tkv, q_pos0, k_sel, got)
+        _call(lib, False, dev_in, Tkv, q_pos0, k_sel, ref)
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):  # same kernels, same inputs: identical outputs
+            assert torch.equal(a.cpu(), b.cpu())
+        _check_vs_oracle(cpu_in, Tkv, q_pos0, k_sel, got[0].cpu(), got[1].cpu())
     assert _lib.device_error() == 0
 
 
 def test_noalloc_refuses_calls_beyond_its_buffer():
     build()
     lib = _lib.load()
-    B, Tq, Tkv = 1, 4096, 4096  # 64 MiB of scores > 16 MiB built in
-    assert lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv) > 16 << 20
-    q, k, w, bias = _inputs(B, Tq, Tkv, 13)
+    B, Tq, Tkv = 1, 2049, 2048  # one row more than the 16 MiB built in
+    assert lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv) > SCRATCH_BYTES
+    q, k, w, bias = (t.cuda() for t in _inputs(B, Tq, Tkv, 13))
     words = lib.gsa_bitmask_words(Tkv)
     _, _, bm = _outputs(B, Tq, 16, words)
+    before = bm.clone()
     rc = lib.gsa_indexer_topk_noalloc(q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1),
                                       w.data_ptr(), w.stride(1), bias.data_ptr(), 0.125, 0, B, Tq,
                                       Tkv, 0, 4, 64, 16, None, None, bm.data_ptr(), words,
                                       torch.cuda.current_stream().cuda_stream)
     assert rc == GSA_ERR_UNSUPPORTED
     assert b"built-in" in lib.gsa_last_error_string()
+    torch.cuda.synchronize()
+    assert torch.equal(bm, before)  # refused before any launch
