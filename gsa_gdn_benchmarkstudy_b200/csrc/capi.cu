@@ -2,6 +2,7 @@
 // checks, TMA tensor-map construction, dispatch to the kernels, status codes.
 #include <cmath>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -131,6 +132,47 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int finish(cudaError_t e) { return e == cudaSuccess ? GSA_OK : set_cuda_error(e); }
 
+// The bf16 tensor-core indexer (indexer_tk.cu) covers H_I = 4, d_I = 64.
+bool tc_path(int dtype, int H_I, int d_I) {
+  return dtype == GSA_DTYPE_BF16 && H_I == 4 && d_I == 64;
+}
+
+// Tensor maps of the tensor-core indexer: q [B, Tq, 256] in boxes of 64 rows
+// of one head; the launch's keys i = 0, 1, ... at sequence rows
+// i * key_step + key_off of k [B, Tkv, 64], in boxes of 128 keys.
+int make_tk_maps(CUtensorMap* qmap, CUtensorMap* kmap, const void* q, int64_t q_stride,
+                 const void* k, int64_t k_stride, int B, int Tq, int Tkv, int key_step,
+                 int key_off) {
+  int rc = make_map_bf16_3d(qmap, q, 256, Tq, B, q_stride * 2,
+                            static_cast<uint64_t>(Tq) * q_stride * 2,
+                            gsa::indexer_tk_rows_per_cta());
+  if (rc) return rc;
+  const int nkeys = (Tkv - key_off + key_step - 1) / key_step;
+  return make_map_bf16_3d(kmap, static_cast<const char*>(k) + static_cast<int64_t>(key_off) *
+                                                                    k_stride * 2,
+                          64, nkeys, B, static_cast<uint64_t>(key_step) * k_stride * 2,
+                          static_cast<uint64_t>(Tkv) * k_stride * 2,
+                          gsa::indexer_tk_keys_per_tile());
+}
+
+gsa::IndexerTkArgs tk_args(const void* w, int64_t w_stride, const float* bias, float scale, int B,
+                           int Tq, int Tkv, int q_pos0, int* err) {
+  gsa::IndexerTkArgs a{};
+  a.w = w;
+  a.w_stride = w_stride;
+  a.bias = bias;
+  a.scale = scale;
+  a.B = B;
+  a.Tq = Tq;
+  a.Tkv = Tkv;
+  a.q_pos0 = q_pos0;
+  a.nkeys = Tkv;
+  a.key_step = 1;
+  a.key_off = 0;
+  a.err = err;
+  return a;
+}
+
 int indexer_impl(const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* w,
                  int64_t w_stride, const float* bias, float scale, int dtype, int B, int Tq,
                  int Tkv, int q_pos0, int H_I, int d_I, float* out, int64_t out_stride,
@@ -151,30 +193,17 @@ int indexer_impl(const void* q, int64_t q_stride, const void* k, int64_t k_strid
     cudaError_t e = gsa::launch_fill_upper(out, out_stride, B, Tq, Tkv, q_pos0, s);
     if (e != cudaSuccess) return set_cuda_error(e);
   }
-  if (dtype == GSA_DTYPE_BF16 && H_I == 4 && d_I == 64) {
+  if (tc_path(dtype, H_I, d_I)) {
     if (!aligned16(q) || !aligned16(k) || (q_stride * 2) % 16 || (k_stride * 2) % 16 ||
         !aligned16(out) || (out_stride * 4) % 16)
       return set_error(GSA_ERR_ALIGNMENT, "indexer rows must be 16-byte aligned");
     CUtensorMap qmap, kmap;
-    rc = make_map_bf16_3d(&qmap, q, static_cast<uint64_t>(H_I) * d_I, Tq, B, q_stride * 2,
-                          static_cast<uint64_t>(Tq) * q_stride * 2, 128);
+    rc = make_tk_maps(&qmap, &kmap, q, q_stride, k, k_stride, B, Tq, Tkv, 1, 0);
     if (rc) return rc;
-    rc = make_map_bf16_3d(&kmap, k, d_I, Tkv, B, k_stride * 2,
-                          static_cast<uint64_t>(Tkv) * k_stride * 2, 32);
-    if (rc) return rc;
-    gsa::IndexerArgs a;
-    a.w = w;
-    a.w_stride = w_stride;
-    a.bias = bias;
-    a.scale = scale;
-    a.B = B;
-    a.Tq = Tq;
-    a.Tkv = Tkv;
-    a.q_pos0 = q_pos0;
+    gsa::IndexerTkArgs a = tk_args(w, w_stride, bias, scale, B, Tq, Tkv, q_pos0, st->err);
     a.out = out;
     a.out_stride = out_stride;
-    a.err = st->err;
-    return finish(gsa::launch_indexer_tc(qmap, kmap, a, s));
+    return finish(gsa::launch_indexer_tk(gsa::kIdxStore, qmap, kmap, a, s));
   }
   if (H_I > 8 || d_I > 128 || H_I * d_I > 512)
     return set_error(GSA_ERR_UNSUPPORTED, "indexer heads/dims beyond the CUDA-core kernel");
@@ -187,11 +216,87 @@ int indexer_impl(const void* q, int64_t q_stride, const void* k, int64_t k_strid
 // Row stride (floats) of the score rows gsa_indexer_topk keeps in its workspace.
 int64_t score_row_stride(int Tkv) { return (static_cast<int64_t>(Tkv) + 3) / 4 * 4; }
 
+// The fused selection samples every kSampleStep-th key of a row to bracket
+// its k-th score, kSampleZ standard deviations of the sample rank wide.
+constexpr int kSampleStep = 8;
+constexpr float kSampleZ = 4.0f;
+
+// The fused selection runs where it pays: the tensor-core indexer, and rows
+// longer than twice k (shorter ones keep most of their keys, and scoring every
+// key into the workspace and selecting from it costs less).
+bool fused_selection(int dtype, int H_I, int d_I, int Tkv, int k_sel) {
+  return tc_path(dtype, H_I, d_I) && Tkv > 2 * k_sel && Tkv >= 4 * kSampleStep;
+}
+
+int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                       const void* w, int64_t w_stride, const float* bias, float scale, int B,
+                       int Tq, int Tkv, int q_pos0, int k_sel, float* ws, int32_t* indices,
+                       uint8_t* mask, uint32_t* bitmask, int64_t bitmask_words, cudaStream_t s) {
+  if (!aligned16(q) || !aligned16(k) || (q_stride * 2) % 16 || (k_stride * 2) % 16 ||
+      !aligned16(ws))
+    return set_error(GSA_ERR_ALIGNMENT, "indexer rows must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const int64_t stride = score_row_stride(Tkv);
+  const int64_t rows = static_cast<int64_t>(B) * Tq;
+  gsa::SelectRowStats* stats = reinterpret_cast<gsa::SelectRowStats*>(ws + rows * stride);
+  const int64_t sel_words = gsa_bitmask_words(Tkv);
+  const int step = kSampleStep, off = kSampleStep - 1;
+  CUtensorMap qmap, kmap, kmap_s, qmap_s;
+  rc = make_tk_maps(&qmap, &kmap, q, q_stride, k, k_stride, B, Tq, Tkv, 1, 0);
+  if (rc) return rc;
+  rc = make_tk_maps(&qmap_s, &kmap_s, q, q_stride, k, k_stride, B, Tq, Tkv, step, off);
+  if (rc) return rc;
+  gsa::IndexerTkArgs a = tk_args(w, w_stride, bias, scale, B, Tq, Tkv, q_pos0, st->err);
+  a.stats = stats;
+  a.k_sel = k_sel;
+  // 1. scores against every step-th key, into the rows' workspace
+  gsa::IndexerTkArgs a1 = a;
+  a1.nkeys = (Tkv - off + step - 1) / step;
+  a1.key_step = step;
+  a1.key_off = off;
+  a1.out = ws;
+  a1.out_stride = stride;
+  cudaError_t e = gsa::launch_indexer_tk(gsa::kIdxSample, qmap_s, kmap_s, a1, s);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  // 2. per-row brackets [lo, hi] of the k-th score
+  e = gsa::launch_select_threshold(ws, stride, B, Tq, Tkv, q_pos0, step, off, k_sel, kSampleZ,
+                                   stats, s);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  // 3. sure bits and candidates, over every key
+  gsa::IndexerTkArgs a3 = a;
+  a3.sel_bits = reinterpret_cast<uint32_t*>(ws);
+  a3.sel_stride = stride;
+  a3.bitmask_words = sel_words;
+  a3.cand_cap = static_cast<int>(
+      std::min<int64_t>(gsa::select_fixup_capacity(), (stride - sel_words) / 2));
+  e = gsa::launch_indexer_tk(gsa::kIdxSelect, qmap, kmap, a3, s);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  // 4. full score rows of the rows whose bracket missed
+  gsa::IndexerTkArgs a4 = a;
+  a4.out = ws;
+  a4.out_stride = stride;
+  e = gsa::launch_indexer_tk(gsa::kIdxStoreFailed, qmap, kmap, a4, s);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  // 5. exact completion of every row
+  return finish(gsa::launch_select_fixup(reinterpret_cast<const uint32_t*>(ws), stride, sel_words,
+                                         stats, B, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
+                                         bitmask_words, s));
+}
+
 int indexer_topk_impl(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                       const void* w, int64_t w_stride, const float* bias, float scale, int dtype,
                       int B, int Tq, int Tkv, int q_pos0, int H_I, int d_I, int k_sel,
                       float* scores, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
                       int64_t bitmask_words, cudaStream_t s) {
+  if (fused_selection(dtype, H_I, d_I, Tkv, k_sel)) {
+    if (!q || !k || !w || !bias) return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+    if (q_stride < static_cast<int64_t>(H_I) * d_I || k_stride < d_I || w_stride < H_I)
+      return set_error(GSA_ERR_INVALID_ARG, "row stride smaller than the row");
+    return indexer_topk_fused(q, q_stride, k, k_stride, w, w_stride, bias, scale, B, Tq, Tkv,
+                              q_pos0, k_sel, scores, indices, mask, bitmask, bitmask_words, s);
+  }
   const int64_t stride = score_row_stride(Tkv);
   int rc = indexer_impl(q, q_stride, k, k_stride, w, w_stride, bias, scale, dtype, B, Tq, Tkv,
                         q_pos0, H_I, d_I, scores, stride, 0, s);
@@ -300,7 +405,9 @@ int gsa_indexer_scores(const void* q, int64_t q_stride, const void* k, int64_t k
 
 int64_t gsa_indexer_topk_workspace_size(int B, int Tq, int Tkv) {
   if (B <= 0 || Tq <= 0 || Tkv <= 0) return 0;
-  return static_cast<int64_t>(B) * Tq * score_row_stride(Tkv) * static_cast<int64_t>(sizeof(float));
+  return static_cast<int64_t>(B) * Tq *
+         (score_row_stride(Tkv) * static_cast<int64_t>(sizeof(float)) +
+          static_cast<int64_t>(sizeof(gsa::SelectRowStats)));
 }
 
 int gsa_indexer_topk(const void* q, int64_t q_stride, const void* k, int64_t k_stride,

@@ -35,6 +35,78 @@ struct IndexerArgs {
 cudaError_t launch_indexer_tc(const CUtensorMap& qmap, const CUtensorMap& kmap,
                               const IndexerArgs& a, cudaStream_t stream);
 
+// ---- tcgen05 indexer with keys as the MMA's M dimension (indexer_tk.cu) and
+// the fused indexer + top-k built on it.
+
+// Per-row state of the fused selection.  The threshold kernel writes hi / lo
+// and zeroes the counters; the kSelect pass adds to the counters.
+struct SelectRowStats {
+  float hi;    // keys scoring above hi are selected outright ("sure")
+  float lo;    // keys scoring in [lo, hi] are candidates
+  int sure;    // number of sure keys
+  int ncand;   // candidates appended to the row's list
+  int flags;   // kSelOverflow
+  int pad[3];
+};
+static_assert(sizeof(SelectRowStats) == 32, "row stats are 32 bytes");
+constexpr int kSelOverflow = 1;
+
+// A row of n causal keys needs the exact fallback when its candidates cannot
+// hold the k-th key: more sure keys than k, fewer sure keys plus candidates
+// than k, or a candidate list that overflowed.  Rows with n <= k select all
+// their keys and never fail.
+__host__ __device__ __forceinline__ bool select_row_failed(const SelectRowStats& st, int n,
+                                                           int k) {
+  if (n <= k) return false;
+  return (st.flags & kSelOverflow) != 0 || st.sure > k || st.sure + st.ncand < k;
+}
+
+enum IndexerTkMode { kIdxStore = 0, kIdxSample = 1, kIdxSelect = 2, kIdxStoreFailed = 3 };
+
+struct IndexerTkArgs {
+  const void* w;           // [B, Tq, 4] bf16, row stride w_stride
+  int64_t w_stride;
+  const float* bias;       // [4]
+  float scale;
+  int B, Tq, Tkv, q_pos0;
+  int nkeys;               // keys of the launch (Tkv, or the number of sampled keys)
+  int key_step, key_off;   // launch key i is sequence key i * key_step + key_off
+  float* out;              // kStore / kSample / kStoreFailed: [B*Tq, out_stride] fp32
+  int64_t out_stride;
+  SelectRowStats* stats;   // kSelect / kStoreFailed: [B*Tq]
+  uint32_t* sel_bits;      // kSelect: row r's sure bits at sel_bits + r*sel_stride,
+  int64_t sel_stride;      //   its candidate list (uint2 {score bits, key}) right after
+  int64_t bitmask_words;   //   the bitmask_words words of bits
+  int cand_cap;            // kSelect: entries of a row's candidate list
+  int k_sel;               // kStoreFailed: k of the failure test
+  int* err;
+};
+// Tensor maps: q box {64, indexer_tk_rows_per_cta()}, k box {64, indexer_tk_keys_per_tile()}.
+int indexer_tk_rows_per_cta();
+int indexer_tk_keys_per_tile();
+cudaError_t launch_indexer_tk(int mode, const CUtensorMap& qmap, const CUtensorMap& kmap,
+                              const IndexerTkArgs& a, cudaStream_t stream);
+
+// Per row: from the row's sampled scores (samples[row * stride + i], i < the
+// row's causal sample count, sample i = key i*key_step + key_off) estimate the
+// k_sel-th score and write hi / lo thresholds around it (z standard
+// deviations of the sample rank on each side) with zeroed counters.
+cudaError_t launch_select_threshold(const float* samples, int64_t stride, int B, int Tq, int Tkv,
+                                    int q_pos0, int key_step, int key_off, int k_sel, float z,
+                                    SelectRowStats* stats, cudaStream_t stream);
+
+// Per row: the exact top-k_sel from the sure bits and candidate list of the
+// kSelect pass (rank among candidates by (score desc, key asc)), or, for rows
+// that failed, from their full score rows (written by kStoreFailed into the
+// same workspace rows).  Outputs as launch_topk.
+cudaError_t launch_select_fixup(const uint32_t* ws, int64_t ws_stride, int64_t sel_words,
+                                const SelectRowStats* stats, int B, int Tq, int Tkv, int q_pos0,
+                                int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                                int64_t bitmask_words, cudaStream_t stream);
+
+// Entries of a row's candidate list that launch_select_fixup can rank.
+int select_fixup_capacity();
+
 // CUDA-core indexer (fp32 or bf16 inputs, any H_I <= 8, d_I <= 128).
 cudaError_t launch_indexer_simt(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                                 const void* w, int64_t w_stride, const float* bias, float scale,

@@ -208,6 +208,44 @@ __device__ __forceinline__ void find_threshold_bin(TopkShared& sh, int krem) {
   __syncthreads();
 }
 
+// Ascending column list (irow) and mask 1 (mrow) of the set bits of
+// sh.bits[0, nwords), in order; every set bit is a finite pick.
+__device__ __forceinline__ void bits_to_lists(TopkShared& sh, int nwords, int32_t* irow,
+                                              uint8_t* mrow) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wseg = (nwords + kTopkWarps - 1) / kTopkWarps;
+  const int w0 = min(warp * wseg, nwords), w1 = min(w0 + wseg, nwords);
+  int cnt = 0;
+  for (int w = w0 + lane; w < w1; w += 32) cnt += __popc(sh.bits[w]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+  if (lane == 0) sh.warp_a[warp] = cnt;
+  __syncthreads();
+  int out = 0;
+  for (int w = 0; w < warp; ++w) out += sh.warp_a[w];
+  for (int wb = w0; wb < w1; wb += 32) {
+    const int w = wb + lane;
+    const uint32_t word = w < w1 ? sh.bits[w] : 0u;
+    const int pc = __popc(word);
+    int incl = pc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int pos = out + incl - pc;
+    uint32_t rest = word;
+    while (rest) {
+      const int bit = __ffs(rest) - 1;
+      rest &= rest - 1;
+      if (irow) irow[pos] = w * 32 + bit;
+      if (mrow) mrow[pos] = 1;
+      ++pos;
+    }
+    out += __shfl_sync(0xFFFFFFFFu, incl, 31);
+  }
+}
+
 // k of one row in adaptive mode (gsa_explained.ipynb, "Adaptive Top-K" cell):
 //   avg_var = mean over the batch's rows of row_var, clamped to >= 1e-6
 //   k = clamp(floor(k_base * avg_var / max(row_var, 1e-6)), k_min, k_max)
@@ -224,28 +262,19 @@ __device__ __forceinline__ int adaptive_row_k(const AdaptiveK& ad, int64_t row) 
   return static_cast<int>(kf);
 }
 
+// Selection of one row (the whole CTA): the k_sel best of the row's n valid
+// scores srow[0, n) into irow / mrow (k_width slots; NULL = not wanted) and
+// brow (bm_words words; NULL = not wanted).
 template <bool kFinite, int kGroups>
-__global__ void __launch_bounds__(kTopkThreads) topk_kernel(
-    const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
-    int k_fixed, int k_width, AdaptiveK ad, int32_t* __restrict__ indices,
-    uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask, int64_t bm_words) {
-  __shared__ TopkShared sh;
-
+__device__ __forceinline__ void topk_row(TopkShared& sh, const float* __restrict__ srow, int n,
+                                         int Tkv, int k_sel, int k_width, int32_t* irow,
+                                         uint8_t* mrow, uint32_t* brow, int64_t bm_words) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
-  const int64_t row = blockIdx.x;  // b * Tq + r
-  const int r = static_cast<int>(row % Tq);
-  const int n = min(q_pos0 + r + 1, Tkv);
-  const float* srow = scores + row * score_stride;
-  int32_t* irow = indices ? indices + row * k_width : nullptr;
-  uint8_t* mrow = mask ? mask + row * k_width : nullptr;
-  uint32_t* brow = bitmask ? bitmask + row * bm_words : nullptr;
   const bool vec_ok = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0;
   const int nwords = (n + 31) / 32;
-  const int k_sel = ad.row_var ? adaptive_row_k(ad, row) : k_fixed;
-  if (ad.row_k && tid == 0) ad.row_k[row] = k_sel;
 
   auto key_at = [&](int j) -> uint32_t { return ord_key(__ldg(srow + j)); };
 
@@ -454,40 +483,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
           for (int64_t w = tid; w < bm_words; w += kTopkThreads)
             brow[w] = w < nwords ? sh.bits[w] : 0u;
         }
-        if (irow || mrow) {
-          // ascending column list from the bitmask; every pick is finite
-          const int wseg = (nwords + kTopkWarps - 1) / kTopkWarps;
-          const int w0 = min(warp * wseg, nwords), w1 = min(w0 + wseg, nwords);
-          int cnt = 0;
-          for (int w = w0 + lane; w < w1; w += 32) cnt += __popc(sh.bits[w]);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
-          if (lane == 0) sh.warp_a[warp] = cnt;
-          __syncthreads();
-          int out = 0;
-          for (int w = 0; w < warp; ++w) out += sh.warp_a[w];
-          for (int wb = w0; wb < w1; wb += 32) {
-            const int w = wb + lane;
-            const uint32_t word = w < w1 ? sh.bits[w] : 0u;
-            const int pc = __popc(word);
-            int incl = pc;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-              if (lane >= o) incl += y;
-            }
-            int pos = out + incl - pc;
-            uint32_t rest = word;
-            while (rest) {
-              const int bit = __ffs(rest) - 1;
-              rest &= rest - 1;
-              if (irow) irow[pos] = w * 32 + bit;
-              if (mrow) mrow[pos] = 1;
-              ++pos;
-            }
-            out += __shfl_sync(0xFFFFFFFFu, incl, 31);
-          }
-        }
+        if (irow || mrow) bits_to_lists(sh, nwords, irow, mrow);
         return true;
       };
       done = lo >= 0x80000000u ? fast(PosBins<kFinite>(lo - 0x80000000u, shift))
@@ -663,6 +659,23 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
   }
 }
 
+template <bool kFinite, int kGroups>
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(
+    const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
+    int k_fixed, int k_width, AdaptiveK ad, int32_t* __restrict__ indices,
+    uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask, int64_t bm_words) {
+  __shared__ TopkShared sh;
+  const int64_t row = blockIdx.x;  // b * Tq + r
+  const int r = static_cast<int>(row % Tq);
+  const int n = min(q_pos0 + r + 1, Tkv);
+  const int k_sel = ad.row_var ? adaptive_row_k(ad, row) : k_fixed;
+  if (ad.row_k && threadIdx.x == 0) ad.row_k[row] = k_sel;
+  topk_row<kFinite, kGroups>(sh, scores + row * score_stride, n, Tkv, k_sel, k_width,
+                             indices ? indices + row * k_width : nullptr,
+                             mask ? mask + row * k_width : nullptr,
+                             bitmask ? bitmask + row * bm_words : nullptr, bm_words);
+}
+
 // ------------------------------------------------------------ row variance
 // Adaptive mode's statistics (gsa_explained.ipynb, "Adaptive Top-K" cell):
 // over the row's valid (finite-or-NaN, i.e. != -inf) scores,
@@ -756,6 +769,199 @@ __global__ void __launch_bounds__(kSumThreads) var_sum_kernel(const float* __res
   if (threadIdx.x == 0) *var_sum = part[0];
 }
 
+// ------------------------------------------------------------ fused selection
+// The selection of gsa_indexer_topk on the tensor-core path (indexer_tk.cu):
+//  1. the indexer scores each row against every key_step-th key (kSample);
+//  2. select_threshold_kernel estimates each row's k-th score from its samples
+//     and brackets it: hi at a sample rank z standard deviations above the
+//     expected rank of the k-th key, lo z standard deviations below;
+//  3. the indexer's kSelect pass turns keys above hi into bitmask bits and
+//     keys in [lo, hi] into a candidate list, scores stored nowhere else;
+//  4. rows whose bracket missed (or whose list overflowed) get their full
+//     score rows (kStoreFailed);
+//  5. select_fixup_kernel completes each row exactly: the best (k - sure) of
+//     its candidates by (score desc, key asc), or the plain top-k of a failed
+//     row's full scores.  Either way the selection equals the top-k of the
+//     same scores.
+constexpr int kFixCap = 2048;  // candidates a row may hold (16 KB of 64-bit keys)
+static_assert(sizeof(int) * kBins + 2 * sizeof(uint32_t) * kCandCap >= 8 * kFixCap,
+              "the fix-up's keys overlay hist + cand_key + cand_idx");
+
+// The float whose order-preserving key (ord_key) is u.
+__device__ __forceinline__ float ord_to_float(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+
+__global__ void __launch_bounds__(kTopkThreads) select_threshold_kernel(
+    const float* __restrict__ samples, int64_t stride, int Tq, int Tkv, int q_pos0, int key_step,
+    int key_off, int k_sel, float z, SelectRowStats* __restrict__ stats) {
+  __shared__ TopkShared sh;
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int pos = q_pos0 + static_cast<int>(row % Tq);
+  const int n = min(pos + 1, Tkv);
+  const float kInf = __int_as_float(0x7F800000);
+  float hi = -kInf, lo = -kInf;  // n <= k: every key is taken (all above hi)
+  if (n > k_sel) {
+    const int n_samples = Tkv > key_off ? (Tkv - key_off + key_step - 1) / key_step : 0;
+    const int m = pos < key_off ? 0 : min((pos - key_off) / key_step + 1, n_samples);
+    hi = kInf;  // without samples every key is a candidate
+    if (m > 0) {
+      // the number of samples above the k-th key follows a hypergeometric law:
+      // mean m*p, variance m*p*(1-p)*(n-m)/(n-1), p = k/n
+      const float p = static_cast<float>(k_sel) / static_cast<float>(n);
+      const float mu = p * static_cast<float>(m);
+      const float var = static_cast<float>(m) * p * (1.f - p) *
+                        static_cast<float>(max(n - m, 0)) / static_cast<float>(max(n - 1, 1));
+      const float sd = sqrtf(var);
+      const int rho_hi = static_cast<int>(floorf(mu - z * sd)) - 1;  // ranks from the top, 1-based
+      const int rho_lo = static_cast<int>(ceilf(mu + z * sd)) + 1;
+      const float* srow = samples + row * stride;
+      uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+      int cnt = 0;
+      for (int i = tid; i < m; i += kTopkThreads) {
+        const uint32_t u = ord_key(srow[i]);
+        kmin = min(kmin, u);
+        kmax = max(kmax, u);
+      }
+      for (int bn = tid; bn < kBins; bn += kTopkThreads) sh.hist[bn] = 0;
+      block_minmax_count(sh, kmin, kmax, cnt);
+      const uint32_t width = kmax - kmin;
+      const int shift = max(0, 32 - __clz(max(width, 1u)) - kDigitBits);
+      for (int i = tid; i < m; i += kTopkThreads)
+        atomicAdd(&sh.hist[(ord_key(srow[i]) - kmin) >> shift], 1);
+      __syncthreads();
+      if (rho_hi >= 1) {  // hi: top edge of the bin holding sample rank rho_hi
+        find_threshold_bin(sh, rho_hi);
+        const uint64_t e = static_cast<uint64_t>(kmin) +
+                           (static_cast<uint64_t>(sh.sh_digit + 1) << shift) - 1u;
+        hi = ord_to_float(static_cast<uint32_t>(min(e, static_cast<uint64_t>(kmax))));
+      }
+      if (rho_lo <= m) {  // lo: bottom edge of the bin holding sample rank rho_lo
+        find_threshold_bin(sh, rho_lo);
+        lo = ord_to_float(kmin + (static_cast<uint32_t>(sh.sh_digit) << shift));
+      }
+    }
+  }
+  if (tid == 0) {
+    SelectRowStats st;
+    st.hi = hi;
+    st.lo = lo;
+    st.sure = 0;
+    st.ncand = 0;
+    st.flags = 0;
+    st.pad[0] = st.pad[1] = st.pad[2] = 0;
+    stats[row] = st;
+  }
+}
+
+// Digit (of 256, counted from the top) holding the rem-th largest key of a
+// class, by warp 0: sets sh_digit, sh_above (keys in higher digits), sh_bin.
+__device__ __forceinline__ void find_digit256(TopkShared& sh, const int* rhist, int rem) {
+  const int lane = threadIdx.x & 31;
+  if ((threadIdx.x >> 5) == 0) {
+    int loc[8], tot = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      loc[q] = rhist[255 - 8 * lane - q];
+      tot += loc[q];
+    }
+    int incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int cum = incl - tot;
+    if (cum < rem && cum + tot >= rem) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (cum < rem && cum + loc[q] >= rem) {
+          sh.sh_digit = 255 - 8 * lane - q;
+          sh.sh_above = cum;
+          sh.sh_bin = loc[q];
+        }
+        cum += loc[q];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+template <int kGroups>
+__global__ void __launch_bounds__(kTopkThreads) select_fixup_kernel(
+    const uint32_t* __restrict__ ws, int64_t ws_stride, int64_t sel_words,
+    const SelectRowStats* __restrict__ stats, int Tq, int Tkv, int q_pos0, int k_sel,
+    int32_t* __restrict__ indices, uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask,
+    int64_t bm_words) {
+  __shared__ TopkShared sh;
+  __shared__ int rhist[256];
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int n = min(q_pos0 + static_cast<int>(row % Tq) + 1, Tkv);
+  const uint32_t* wrow = ws + row * ws_stride;
+  int32_t* irow = indices ? indices + row * k_sel : nullptr;
+  uint8_t* mrow = mask ? mask + row * k_sel : nullptr;
+  uint32_t* brow = bitmask ? bitmask + row * bm_words : nullptr;
+  const SelectRowStats st = stats[row];
+  if (n <= k_sel || select_row_failed(st, n, k_sel)) {
+    // every key (no score is read), or the plain top-k of the full score row
+    topk_row<true, kGroups>(sh, reinterpret_cast<const float*>(wrow), n, Tkv, k_sel, k_sel, irow,
+                            mrow, brow, bm_words);
+    return;
+  }
+  const int nwords = (n + 31) / 32;
+  for (int w = tid; w < nwords; w += kTopkThreads) sh.bits[w] = wrow[w];
+  const int need = k_sel - st.sure;  // 0 <= need <= ncand (the row did not fail)
+  const int nc = st.ncand;
+  const uint2* cand = reinterpret_cast<const uint2*>(wrow + sel_words);
+  __syncthreads();
+  if (need > 0 && need >= nc) {
+    for (int c = tid; c < nc; c += kTopkThreads) {
+      const uint32_t j = cand[c].y;
+      atomicOr(&sh.bits[j >> 5], 1u << (j & 31));
+    }
+  } else if (need > 0) {
+    // the need best candidates by (score desc, key asc): the need largest of
+    // the distinct 64-bit keys ord_key(score) << 32 | (2^32 - 1 - key), by an
+    // MSB-first radix select, 8 bits per pass
+    uint64_t* key = reinterpret_cast<uint64_t*>(sh.hist);
+    for (int c = tid; c < nc; c += kTopkThreads) {
+      const uint2 e = cand[c];
+      key[c] = (static_cast<uint64_t>(ord_key(__uint_as_float(e.x))) << 32) | (0xFFFFFFFFu - e.y);
+    }
+    uint64_t prefix = 0, pmask = 0;
+    int rem = need;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int bn = tid; bn < 256; bn += kTopkThreads) rhist[bn] = 0;
+      __syncthreads();
+      for (int c = tid; c < nc; c += kTopkThreads) {
+        const uint64_t K = key[c];
+        if ((K & pmask) == prefix) atomicAdd(&rhist[(K >> shift) & 255u], 1);
+      }
+      __syncthreads();
+      find_digit256(sh, rhist, rem);
+      const int bin = sh.sh_bin;
+      rem -= sh.sh_above;
+      prefix |= static_cast<uint64_t>(sh.sh_digit) << shift;
+      pmask |= static_cast<uint64_t>(0xFFu) << shift;
+      __syncthreads();  // every thread has read sh_* before the next pass rewrites it
+      if (bin == rem) break;  // the rest of the class is taken whole
+    }
+    for (int c = tid; c < nc; c += kTopkThreads) {
+      const uint64_t K = key[c];
+      if ((K & pmask) >= prefix) {
+        const uint32_t j = 0xFFFFFFFFu - static_cast<uint32_t>(K);
+        atomicOr(&sh.bits[j >> 5], 1u << (j & 31));
+      }
+    }
+  }
+  __syncthreads();
+  if (brow)
+    for (int64_t w = tid; w < bm_words; w += kTopkThreads) brow[w] = w < nwords ? sh.bits[w] : 0u;
+  if (irow || mrow) bits_to_lists(sh, nwords, irow, mrow);
+}
+
 }  // namespace
 
 cudaError_t launch_topk(const float* scores, int64_t score_stride, int B, int Tq, int Tkv,
@@ -785,5 +991,31 @@ cudaError_t launch_row_variance(const float* scores, int64_t score_stride, int B
   var_sum_kernel<<<1, kSumThreads, 0, stream>>>(row_var, rows, var_sum);
   return cudaGetLastError();
 }
+
+cudaError_t launch_select_threshold(const float* samples, int64_t stride, int B, int Tq, int Tkv,
+                                    int q_pos0, int key_step, int key_off, int k_sel, float z,
+                                    SelectRowStats* stats, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(B) * Tq;
+  if (rows == 0) return cudaSuccess;
+  select_threshold_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+      samples, stride, Tq, Tkv, q_pos0, key_step, key_off, k_sel, z, stats);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select_fixup(const uint32_t* ws, int64_t ws_stride, int64_t sel_words,
+                                const SelectRowStats* stats, int B, int Tq, int Tkv, int q_pos0,
+                                int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
+                                int64_t bitmask_words, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(B) * Tq;
+  if (rows == 0) return cudaSuccess;
+  auto kernel = Tkv >= kLongKeyRange ? select_fixup_kernel<kEmitLong>
+                                     : select_fixup_kernel<kEmitShort>;
+  kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+      ws, ws_stride, sel_words, stats, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
+      bitmask_words);
+  return cudaGetLastError();
+}
+
+int select_fixup_capacity() { return kFixCap; }
 
 }  // namespace gsa
