@@ -6,6 +6,7 @@ not an sm_100 GPU, every call raises ``RuntimeError``.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import threading
 from pathlib import Path
@@ -15,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libgsa_b200.so"
 GSA_OK = 0
 GSA_DTYPE_BF16 = 0
 GSA_DTYPE_F32 = 1
+GSA_FUSED_AUTO, GSA_FUSED_ALWAYS, GSA_FUSED_NEVER = 0, 1, 2
 
 # Every exported symbol of include/gsa_b200.h with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -23,6 +25,7 @@ _i64 = ctypes.c_int64
 _f32 = ctypes.c_float
 SIGNATURES: dict[str, tuple] = {
     "gsa_version": (_i32, []),
+    "gsa_set_fused_selection": (_i32, [_i32]),
     "gsa_status_string": (ctypes.c_char_p, [_i32]),
     "gsa_last_error_string": (ctypes.c_char_p, []),
     "gsa_device_error": (_i32, [ctypes.POINTER(_i32), _i32]),
@@ -127,3 +130,15 @@ def device_error(reset: bool = True) -> int:
     out = ctypes.c_int(0)
     check(load().gsa_device_error(ctypes.byref(out), 1 if reset else 0), "gsa_device_error")
     return out.value
+
+
+@contextlib.contextmanager
+def fused_selection(mode: int):
+    """Inside the block, gsa_indexer_topk uses the given selection
+    (GSA_FUSED_ALWAYS / GSA_FUSED_NEVER / GSA_FUSED_AUTO) process-wide; the
+    automatic choice is restored afterwards."""
+    check(load().gsa_set_fused_selection(int(mode)), "gsa_set_fused_selection")
+    try:
+        yield
+    finally:
+        check(load().gsa_set_fused_selection(GSA_FUSED_AUTO), "gsa_set_fused_selection")

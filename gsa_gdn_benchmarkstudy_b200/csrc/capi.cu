@@ -145,7 +145,7 @@ int make_tk_maps(CUtensorMap* qmap, CUtensorMap* kmap, const void* q, int64_t q_
                  int key_off) {
   int rc = make_map_bf16_3d(qmap, q, 256, Tq, B, q_stride * 2,
                             static_cast<uint64_t>(Tq) * q_stride * 2,
-                            gsa::indexer_tk_rows_per_cta());
+                            gsa::indexer_tk_rows_per_cta());  // one box per head
   if (rc) return rc;
   const int nkeys = (Tkv - key_off + key_step - 1) / key_step;
   return make_map_bf16_3d(kmap, static_cast<const char*>(k) + static_cast<int64_t>(key_off) *
@@ -221,11 +221,50 @@ int64_t score_row_stride(int Tkv) { return (static_cast<int64_t>(Tkv) + 3) / 4 *
 constexpr int kSampleStep = 8;
 constexpr float kSampleZ = 4.0f;
 
-// The fused selection runs where it pays: the tensor-core indexer, and rows
-// longer than twice k (shorter ones keep most of their keys, and scoring every
-// key into the workspace and selecting from it costs less).
+// Selection state of one workspace row (stride words): the sure bits in the
+// first gsa_bitmask_words(Tkv) words, one count per candidate list (two lists
+// per indexer key chunk: the 16-key halves of its 32-key sub-tiles), then the
+// lists, each of
+// *per_list entries of two words, from word *cand_off on.  A list holds up to
+// kMaxPerList candidates (nearly half of its 256 keys) where the row has room.
+constexpr int kMaxPerList = 120;
+void selection_layout(int Tkv, int64_t* cand_off, int* per_list) {
+  const int64_t stride = score_row_stride(Tkv);
+  const int64_t lists = 2 * ((static_cast<int64_t>(Tkv) + gsa::indexer_tk_keys_per_cta() - 1) /
+                             gsa::indexer_tk_keys_per_cta());
+  // lists start on 16-byte boundaries and hold an even number of entries: the
+  // fix-up reads each with one bulk copy
+  const int64_t off = (gsa_bitmask_words(Tkv) + lists + 3) / 4 * 4;
+  *cand_off = off;
+  *per_list =
+      static_cast<int>(std::min<int64_t>(kMaxPerList, (stride - off) / (2 * lists))) & ~1;
+}
+
+// gsa_set_fused_selection's mode (GSA_FUSED_AUTO by default).
+std::atomic<int> g_fused_mode{GSA_FUSED_AUTO};
+
+// Where the fused selection applies at all: the tensor-core indexer, rows
+// longer than twice k, at most kSelMaxKeys keys, room for the candidate lists.
+bool fused_possible(int dtype, int H_I, int d_I, int Tkv, int k_sel) {
+  if (!tc_path(dtype, H_I, d_I) || Tkv <= 2 * k_sel || Tkv < 4 * kSampleStep ||
+      Tkv > gsa::kSelMaxKeys)
+    return false;
+  int64_t cand_off = 0;
+  int per_list = 0;
+  selection_layout(Tkv, &cand_off, &per_list);
+  return per_list >= 8;
+}
+
+// The automatic choice takes the fused selection where it measured faster on
+// B200: key ranges of at least kFusedMinRatio * k (T = 65536, k = 2048: 5.86
+// against 6.59 ms for indexer + top-k; T = 16384: 0.52 against 0.51 ms;
+// B = 8, T = 8192: 1.25 against 1.09 ms).
+constexpr int kFusedMinRatio = 16;
 bool fused_selection(int dtype, int H_I, int d_I, int Tkv, int k_sel) {
-  return tc_path(dtype, H_I, d_I) && Tkv > 2 * k_sel && Tkv >= 4 * kSampleStep;
+  const int mode = g_fused_mode.load(std::memory_order_relaxed);
+  if (mode == GSA_FUSED_NEVER || !fused_possible(dtype, H_I, d_I, Tkv, k_sel)) return false;
+  return mode == GSA_FUSED_ALWAYS ||
+         static_cast<int64_t>(Tkv) >= static_cast<int64_t>(kFusedMinRatio) * k_sel;
 }
 
 int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
@@ -243,6 +282,9 @@ int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k
   gsa::SelectRowStats* stats = reinterpret_cast<gsa::SelectRowStats*>(ws + rows * stride);
   const int64_t sel_words = gsa_bitmask_words(Tkv);
   const int step = kSampleStep, off = kSampleStep - 1;
+  int64_t cand_off = 0;
+  int per_list = 0;
+  selection_layout(Tkv, &cand_off, &per_list);
   CUtensorMap qmap, kmap, kmap_s, qmap_s;
   rc = make_tk_maps(&qmap, &kmap, q, q_stride, k, k_stride, B, Tq, Tkv, 1, 0);
   if (rc) return rc;
@@ -269,11 +311,13 @@ int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k
   a3.sel_bits = reinterpret_cast<uint32_t*>(ws);
   a3.sel_stride = stride;
   a3.bitmask_words = sel_words;
-  a3.cand_cap = static_cast<int>(
-      std::min<int64_t>(gsa::select_fixup_capacity(), (stride - sel_words) / 2));
+  a3.cand_off = cand_off;
+  a3.cand_per_list = per_list;
   e = gsa::launch_indexer_tk(gsa::kIdxSelect, qmap, kmap, a3, s);
   if (e != cudaSuccess) return set_cuda_error(e);
   // 4. full score rows of the rows whose bracket missed
+  e = gsa::launch_select_scan(stats, B, Tq, Tkv, q_pos0, k_sel, gsa::indexer_tk_rows_per_cta(), s);
+  if (e != cudaSuccess) return set_cuda_error(e);
   gsa::IndexerTkArgs a4 = a;
   a4.out = ws;
   a4.out_stride = stride;
@@ -281,8 +325,9 @@ int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k
   if (e != cudaSuccess) return set_cuda_error(e);
   // 5. exact completion of every row
   return finish(gsa::launch_select_fixup(reinterpret_cast<const uint32_t*>(ws), stride, sel_words,
+                                         cand_off, per_list, gsa::indexer_tk_keys_per_cta(),
                                          stats, B, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
-                                         bitmask_words, s));
+                                         bitmask_words, st->err, s));
 }
 
 int indexer_topk_impl(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
@@ -330,6 +375,13 @@ int check_adaptive_k(int k_base, int k_min, int k_max) {
 extern "C" {
 
 int gsa_version(void) { return kVersion; }
+
+int gsa_set_fused_selection(int mode) {
+  if (mode != GSA_FUSED_AUTO && mode != GSA_FUSED_ALWAYS && mode != GSA_FUSED_NEVER)
+    return set_error(GSA_ERR_INVALID_ARG, "mode must be GSA_FUSED_AUTO, _ALWAYS or _NEVER");
+  g_fused_mode.store(mode, std::memory_order_relaxed);
+  return GSA_OK;
+}
 
 const char* gsa_status_string(int status) {
   switch (status) {

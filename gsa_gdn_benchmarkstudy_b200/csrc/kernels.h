@@ -20,21 +20,6 @@ cudaError_t launch_output_gate(const void* o, int64_t o_stride, const void* og, 
                                void* out, int64_t out_stride, int dtype, int rows, int width,
                                cudaStream_t stream);
 
-// Tensor-core indexer (bf16, H_I = 4, d_I = 64).  Tensor maps are built by
-// the caller (capi.cu).
-struct IndexerArgs {
-  const void* w;
-  int64_t w_stride;
-  const float* bias;
-  float scale;
-  int B, Tq, Tkv, q_pos0;
-  float* out;
-  int64_t out_stride;
-  int* err;
-};
-cudaError_t launch_indexer_tc(const CUtensorMap& qmap, const CUtensorMap& kmap,
-                              const IndexerArgs& a, cudaStream_t stream);
-
 // ---- tcgen05 indexer with keys as the MMA's M dimension (indexer_tk.cu) and
 // the fused indexer + top-k built on it.
 
@@ -46,19 +31,22 @@ struct SelectRowStats {
   int sure;    // number of sure keys
   int ncand;   // candidates appended to the row's list
   int flags;   // kSelOverflow
-  int pad[3];
+  int pad[3];  // pad[0] of an indexer tile's first row: some row of the tile failed
 };
 static_assert(sizeof(SelectRowStats) == 32, "row stats are 32 bytes");
 constexpr int kSelOverflow = 1;
+constexpr int kSelCandCap = 2048;  // candidates of a row the fix-up can rank
+constexpr int kSelMaxKeys = 65536;  // longest row of the fused selection (its bitmask in shared memory)
 
 // A row of n causal keys needs the exact fallback when its candidates cannot
 // hold the k-th key: more sure keys than k, fewer sure keys plus candidates
-// than k, or a candidate list that overflowed.  Rows with n <= k select all
-// their keys and never fail.
+// than k, a candidate list that overflowed, or more candidates than the
+// fix-up ranks.  Rows with n <= k select all their keys and never fail.
 __host__ __device__ __forceinline__ bool select_row_failed(const SelectRowStats& st, int n,
                                                            int k) {
   if (n <= k) return false;
-  return (st.flags & kSelOverflow) != 0 || st.sure > k || st.sure + st.ncand < k;
+  return (st.flags & kSelOverflow) != 0 || st.sure > k || st.sure + st.ncand < k ||
+         st.ncand > kSelCandCap;
 }
 
 enum IndexerTkMode { kIdxStore = 0, kIdxSample = 1, kIdxSelect = 2, kIdxStoreFailed = 3 };
@@ -74,16 +62,24 @@ struct IndexerTkArgs {
   float* out;              // kStore / kSample / kStoreFailed: [B*Tq, out_stride] fp32
   int64_t out_stride;
   SelectRowStats* stats;   // kSelect / kStoreFailed: [B*Tq]
-  uint32_t* sel_bits;      // kSelect: row r's sure bits at sel_bits + r*sel_stride,
-  int64_t sel_stride;      //   its candidate list (uint2 {score bits, key}) right after
-  int64_t bitmask_words;   //   the bitmask_words words of bits
-  int cand_cap;            // kSelect: entries of a row's candidate list
+  // kSelect: the selection state of row r lives in the words
+  // sel_bits[r*sel_stride, +sel_stride): its sure bits in [0, bitmask_words),
+  // the candidate count of list l = 2 * (key chunk) + (chunk half) at
+  // bitmask_words + l, and list l's cand_per_list entries (uint2 {score bits,
+  // key}) from word cand_off + 2 * l * cand_per_list on.
+  uint32_t* sel_bits;
+  int64_t sel_stride;
+  int64_t bitmask_words;
+  int64_t cand_off;
+  int cand_per_list;
   int k_sel;               // kStoreFailed: k of the failure test
   int* err;
 };
 // Tensor maps: q box {64, indexer_tk_rows_per_cta()}, k box {64, indexer_tk_keys_per_tile()}.
+// A CTA covers indexer_tk_keys_per_cta() launch keys: two candidate lists.
 int indexer_tk_rows_per_cta();
 int indexer_tk_keys_per_tile();
+int indexer_tk_keys_per_cta();
 cudaError_t launch_indexer_tk(int mode, const CUtensorMap& qmap, const CUtensorMap& kmap,
                               const IndexerTkArgs& a, cudaStream_t stream);
 
@@ -95,17 +91,21 @@ cudaError_t launch_select_threshold(const float* samples, int64_t stride, int B,
                                     int q_pos0, int key_step, int key_off, int k_sel, float z,
                                     SelectRowStats* stats, cudaStream_t stream);
 
-// Per row: the exact top-k_sel from the sure bits and candidate list of the
+// After the kSelect pass: marks, for kStoreFailed, each indexer tile of
+// tile_rows rows that holds a failed row (in stats[first row of tile].pad[0]).
+cudaError_t launch_select_scan(SelectRowStats* stats, int B, int Tq, int Tkv, int q_pos0,
+                               int k_sel, int tile_rows, cudaStream_t stream);
+
+// Per row: the exact top-k_sel from the sure bits and candidate lists of the
 // kSelect pass (rank among candidates by (score desc, key asc)), or, for rows
 // that failed, from their full score rows (written by kStoreFailed into the
-// same workspace rows).  Outputs as launch_topk.
+// same workspace rows).  Outputs as launch_topk.  The lists are read with bulk
+// copies: cand_off must be a multiple of 4 words and cand_per_list even.
 cudaError_t launch_select_fixup(const uint32_t* ws, int64_t ws_stride, int64_t sel_words,
+                                int64_t cand_off, int cand_per_list, int keys_per_chunk,
                                 const SelectRowStats* stats, int B, int Tq, int Tkv, int q_pos0,
                                 int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
-                                int64_t bitmask_words, cudaStream_t stream);
-
-// Entries of a row's candidate list that launch_select_fixup can rank.
-int select_fixup_capacity();
+                                int64_t bitmask_words, int* err, cudaStream_t stream);
 
 // CUDA-core indexer (fp32 or bf16 inputs, any H_I <= 8, d_I <= 128).
 cudaError_t launch_indexer_simt(const void* q, int64_t q_stride, const void* k, int64_t k_stride,

@@ -28,6 +28,7 @@
 // exact path: an MSB-first 11-bit radix select starting at the highest bit in
 // which the row's min and max keys differ, with candidate compaction, and a
 // warp-segmented emit.  Both paths implement the same selection rule.
+#include <algorithm>
 #include <type_traits>
 
 #include "kernels.h"
@@ -145,7 +146,8 @@ struct alignas(16) TopkShared {
 };
 
 // Block-wide reduction of (min, max, sum) into every thread.
-__device__ __forceinline__ void block_minmax_count(TopkShared& sh, uint32_t& kmin, uint32_t& kmax,
+template <typename Sh>
+__device__ __forceinline__ void block_minmax_count(Sh& sh, uint32_t& kmin, uint32_t& kmax,
                                                    int& cnt) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -174,13 +176,14 @@ __device__ __forceinline__ void block_minmax_count(TopkShared& sh, uint32_t& kmi
 
 // Suffix scan over sh.hist (bins counted from the top down): finds the bin
 // holding the krem-th largest key; sets sh_digit / sh_above / sh_bin.
-__device__ __forceinline__ void find_threshold_bin(TopkShared& sh, int krem) {
+template <int kNB = kBins, typename Sh>
+__device__ __forceinline__ void find_threshold_bin(Sh& sh, int krem) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int kBpt = kBins / kTopkThreads;
+  constexpr int kBpt = kNB / kTopkThreads;
   int own[kBpt], loc = 0;
 #pragma unroll
   for (int q = 0; q < kBpt; ++q) {
-    own[q] = sh.hist[kBins - 1 - (kBpt * tid + q)];
+    own[q] = sh.hist[kNB - 1 - (kBpt * tid + q)];
     loc += own[q];
   }
   int inc = loc;
@@ -198,7 +201,7 @@ __device__ __forceinline__ void find_threshold_bin(TopkShared& sh, int krem) {
 #pragma unroll
     for (int q = 0; q < kBpt; ++q) {
       if (cum < krem && cum + own[q] >= krem) {
-        sh.sh_digit = kBins - 1 - (kBpt * tid + q);
+        sh.sh_digit = kNB - 1 - (kBpt * tid + q);
         sh.sh_above = cum;
         sh.sh_bin = own[q];
       }
@@ -210,7 +213,8 @@ __device__ __forceinline__ void find_threshold_bin(TopkShared& sh, int krem) {
 
 // Ascending column list (irow) and mask 1 (mrow) of the set bits of
 // sh.bits[0, nwords), in order; every set bit is a finite pick.
-__device__ __forceinline__ void bits_to_lists(TopkShared& sh, int nwords, int32_t* irow,
+template <typename Sh>
+__device__ __forceinline__ void bits_to_lists(Sh& sh, int nwords, int32_t* irow,
                                               uint8_t* mrow) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int wseg = (nwords + kTopkWarps - 1) / kTopkWarps;
@@ -776,28 +780,61 @@ __global__ void __launch_bounds__(kSumThreads) var_sum_kernel(const float* __res
 //     and brackets it: hi at a sample rank z standard deviations above the
 //     expected rank of the k-th key, lo z standard deviations below;
 //  3. the indexer's kSelect pass turns keys above hi into bitmask bits and
-//     keys in [lo, hi] into a candidate list, scores stored nowhere else;
-//  4. rows whose bracket missed (or whose list overflowed) get their full
+//     keys in [lo, hi] into candidate lists, scores stored nowhere else;
+//  4. rows whose bracket missed (or whose lists overflowed) get their full
 //     score rows (kStoreFailed);
 //  5. select_fixup_kernel completes each row exactly: the best (k - sure) of
 //     its candidates by (score desc, key asc), or the plain top-k of a failed
 //     row's full scores.  Either way the selection equals the top-k of the
 //     same scores.
-constexpr int kFixCap = 2048;  // candidates a row may hold (16 KB of 64-bit keys)
-static_assert(sizeof(int) * kBins + 2 * sizeof(uint32_t) * kCandCap >= 8 * kFixCap,
-              "the fix-up's keys overlay hist + cand_key + cand_idx");
+constexpr int kFixCap = kSelCandCap;  // candidates a row may hold
+constexpr int kThrRows = kTopkWarps;  // threshold kernel: one warp per row
+constexpr int kThrBins = 256;
 
 // The float whose order-preserving key (ord_key) is u.
 __device__ __forceinline__ float ord_to_float(uint32_t u) {
   return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
 }
 
+// Bin (of kThrBins, counted from the top by one warp) holding the rank-th
+// largest sample, and the samples in higher bins.
+__device__ __forceinline__ int warp_rank_bin(const int* hist, int rank, int& above) {
+  const int lane = threadIdx.x & 31;
+  int loc[kThrBins / 32], tot = 0;
+#pragma unroll
+  for (int q = 0; q < kThrBins / 32; ++q) {
+    loc[q] = hist[kThrBins - 1 - (kThrBins / 32) * lane - q];
+    tot += loc[q];
+  }
+  int incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int cum = incl - tot, bin = -1, ab = 0;
+#pragma unroll
+  for (int q = 0; q < kThrBins / 32; ++q) {
+    if (cum < rank && cum + loc[q] >= rank) {
+      bin = kThrBins - 1 - (kThrBins / 32) * lane - q;
+      ab = cum;
+    }
+    cum += loc[q];
+  }
+  const uint32_t who = __ballot_sync(0xFFFFFFFFu, bin >= 0);
+  const int src = who ? __ffs(who) - 1 : 0;
+  above = __shfl_sync(0xFFFFFFFFu, ab, src);
+  return __shfl_sync(0xFFFFFFFFu, bin, src);
+}
+
 __global__ void __launch_bounds__(kTopkThreads) select_threshold_kernel(
-    const float* __restrict__ samples, int64_t stride, int Tq, int Tkv, int q_pos0, int key_step,
-    int key_off, int k_sel, float z, SelectRowStats* __restrict__ stats) {
-  __shared__ TopkShared sh;
-  const int tid = threadIdx.x;
-  const int64_t row = blockIdx.x;
+    const float* __restrict__ samples, int64_t stride, int64_t rows, int Tq, int Tkv, int q_pos0,
+    int key_step, int key_off, int k_sel, float z, SelectRowStats* __restrict__ stats) {
+  __shared__ int hist_all[kThrRows][kThrBins];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kThrRows + warp;
+  if (row >= rows) return;  // warp-uniform; no block-wide barrier below
+  int* hist = hist_all[warp];
   const int pos = q_pos0 + static_cast<int>(row % Tq);
   const int n = min(pos + 1, Tkv);
   const float kInf = __int_as_float(0x7F800000);
@@ -818,32 +855,35 @@ __global__ void __launch_bounds__(kTopkThreads) select_threshold_kernel(
       const int rho_lo = static_cast<int>(ceilf(mu + z * sd)) + 1;
       const float* srow = samples + row * stride;
       uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-      int cnt = 0;
-      for (int i = tid; i < m; i += kTopkThreads) {
+      for (int i = lane; i < m; i += 32) {
         const uint32_t u = ord_key(srow[i]);
         kmin = min(kmin, u);
         kmax = max(kmax, u);
       }
-      for (int bn = tid; bn < kBins; bn += kTopkThreads) sh.hist[bn] = 0;
-      block_minmax_count(sh, kmin, kmax, cnt);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(0xFFFFFFFFu, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(0xFFFFFFFFu, kmax, o));
+      }
+      for (int bn = lane; bn < kThrBins; bn += 32) hist[bn] = 0;
+      __syncwarp();
       const uint32_t width = kmax - kmin;
-      const int shift = max(0, 32 - __clz(max(width, 1u)) - kDigitBits);
-      for (int i = tid; i < m; i += kTopkThreads)
-        atomicAdd(&sh.hist[(ord_key(srow[i]) - kmin) >> shift], 1);
-      __syncthreads();
+      const int shift = max(0, 32 - __clz(max(width, 1u)) - 8);  // (width >> shift) < 256
+      for (int i = lane; i < m; i += 32) atomicAdd(&hist[(ord_key(srow[i]) - kmin) >> shift], 1);
+      __syncwarp();
+      int above = 0;
       if (rho_hi >= 1) {  // hi: top edge of the bin holding sample rank rho_hi
-        find_threshold_bin(sh, rho_hi);
-        const uint64_t e = static_cast<uint64_t>(kmin) +
-                           (static_cast<uint64_t>(sh.sh_digit + 1) << shift) - 1u;
+        const int bn = warp_rank_bin(hist, rho_hi, above);
+        const uint64_t e = static_cast<uint64_t>(kmin) + (static_cast<uint64_t>(bn + 1) << shift) - 1u;
         hi = ord_to_float(static_cast<uint32_t>(min(e, static_cast<uint64_t>(kmax))));
       }
       if (rho_lo <= m) {  // lo: bottom edge of the bin holding sample rank rho_lo
-        find_threshold_bin(sh, rho_lo);
-        lo = ord_to_float(kmin + (static_cast<uint32_t>(sh.sh_digit) << shift));
+        const int bn = warp_rank_bin(hist, rho_lo, above);
+        lo = ord_to_float(kmin + (static_cast<uint32_t>(bn) << shift));
       }
     }
   }
-  if (tid == 0) {
+  if (lane == 0) {
     SelectRowStats st;
     st.hi = hi;
     st.lo = lo;
@@ -855,111 +895,228 @@ __global__ void __launch_bounds__(kTopkThreads) select_threshold_kernel(
   }
 }
 
-// Digit (of 256, counted from the top) holding the rem-th largest key of a
-// class, by warp 0: sets sh_digit, sh_above (keys in higher digits), sh_bin.
-__device__ __forceinline__ void find_digit256(TopkShared& sh, const int* rhist, int rem) {
-  const int lane = threadIdx.x & 31;
-  if ((threadIdx.x >> 5) == 0) {
-    int loc[8], tot = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      loc[q] = rhist[255 - 8 * lane - q];
-      tot += loc[q];
-    }
-    int incl = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    int cum = incl - tot;
-    if (cum < rem && cum + tot >= rem) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (cum < rem && cum + loc[q] >= rem) {
-          sh.sh_digit = 255 - 8 * lane - q;
-          sh.sh_above = cum;
-          sh.sh_bin = loc[q];
-        }
-        cum += loc[q];
-      }
-    }
-  }
-  __syncthreads();
+// One thread per row: marks the indexer tile (tile_rows rows) of every failed
+// row in the `pad[0]` word of the tile's first row, so that kStoreFailed CTAs
+// of tiles without a failed row read one word and exit.
+__global__ void __launch_bounds__(256) select_scan_kernel(SelectRowStats* __restrict__ stats,
+                                                         int64_t rows, int Tq, int Tkv,
+                                                         int q_pos0, int k_sel, int tile_rows) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int r = static_cast<int>(row % Tq);
+  const int n = min(q_pos0 + r + 1, Tkv);
+  if (select_row_failed(stats[row], n, k_sel)) atomicOr(&stats[row - r % tile_rows].pad[0], 1);
 }
 
-template <int kGroups>
-__global__ void __launch_bounds__(kTopkThreads) select_fixup_kernel(
-    const uint32_t* __restrict__ ws, int64_t ws_stride, int64_t sel_words,
-    const SelectRowStats* __restrict__ stats, int Tq, int Tkv, int q_pos0, int k_sel,
-    int32_t* __restrict__ indices, uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask,
-    int64_t bm_words) {
-  __shared__ TopkShared sh;
-  __shared__ int rhist[256];
-  const int tid = threadIdx.x;
+// Shared memory of the fix-up (rows that did not fail).
+constexpr int kFixLists = kSelMaxKeys / 256;  // lists of the longest row
+constexpr int kFixBins = 512;                 // 9-bit digits of the candidate keys
+constexpr int kFixDigit = 9;
+constexpr int kFixLevels = 4;                 // 4 x 9 bits cover a 32-bit key
+struct alignas(16) FixupShared {
+  uint2 cand[kFixCap + kFixLists];  // the row's lists, each padded to an even length
+  int hist[kFixBins];               // histogram of a digit of the candidate keys
+  int last[kFixCap];                // columns of the last bin's members (one key value)
+  uint32_t bits[kMaxWords];
+  int warp_a[kTopkWarps];
+  uint64_t bar;                     // completion of the lists' bulk copies
+  int abort;
+  int neq;
+  int sh_digit, sh_above, sh_bin;
+};
+constexpr uint32_t kNoKey = 0xFFFFFFFFu;  // column of a padding slot
+
+// Rows that did not fail (and rows with n <= k): the k best keys are the sure
+// bits plus the need = k - sure best candidates by (score desc, key asc).
+// Failed rows are left to select_fallback_kernel.
+__global__ void __launch_bounds__(kTopkThreads, 6) select_fixup_kernel(
+    const uint32_t* __restrict__ ws, int64_t ws_stride, int64_t sel_words, int64_t cand_off,
+    int cand_per_list, int keys_per_chunk, const SelectRowStats* __restrict__ stats, int Tq,
+    int Tkv, int q_pos0, int k_sel, int32_t* __restrict__ indices, uint8_t* __restrict__ mask,
+    uint32_t* __restrict__ bitmask, int64_t bm_words, int* err) {
+  __shared__ FixupShared sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = blockIdx.x;
   const int n = min(q_pos0 + static_cast<int>(row % Tq) + 1, Tkv);
   const uint32_t* wrow = ws + row * ws_stride;
   int32_t* irow = indices ? indices + row * k_sel : nullptr;
   uint8_t* mrow = mask ? mask + row * k_sel : nullptr;
   uint32_t* brow = bitmask ? bitmask + row * bm_words : nullptr;
-  const SelectRowStats st = stats[row];
-  if (n <= k_sel || select_row_failed(st, n, k_sel)) {
-    // every key (no score is read), or the plain top-k of the full score row
-    topk_row<true, kGroups>(sh, reinterpret_cast<const float*>(wrow), n, Tkv, k_sel, k_sel, irow,
-                            mrow, brow, bm_words);
+  const int nwords = (n + 31) / 32;
+  if (n <= k_sel) {  // every key of the row (no score is read)
+    const int full = n >> 5, rem_bits = n & 31;
+    if (brow)
+      for (int64_t w = tid; w < bm_words; w += kTopkThreads)
+        brow[w] = w < full ? 0xFFFFFFFFu : (w == full && rem_bits ? (1u << rem_bits) - 1u : 0u);
+    for (int s = tid; s < k_sel; s += kTopkThreads) {
+      if (irow) irow[s] = min(s, Tkv - 1);  // s itself below n; filler above
+      if (mrow) mrow[s] = s < n ? 1 : 0;
+    }
     return;
   }
-  const int nwords = (n + 31) / 32;
+  // the row's counters, sure bits and list counts are read together (one round
+  // trip): candidates of every list holding a key of the row, two lists per key
+  // chunk (the two interleaved halves), each count <= cand_per_list
+  const int nlists = 2 * ((n + keys_per_chunk - 1) / keys_per_chunk);
+  const uint2* lists = reinterpret_cast<const uint2*>(wrow + cand_off);
+  int c0 = 0, c1 = 0;  // counts of lists 2*tid and 2*tid+1
+  if (2 * tid < nlists) c0 = static_cast<int>(wrow[sel_words + 2 * tid]);
+  if (2 * tid + 1 < nlists) c1 = static_cast<int>(wrow[sel_words + 2 * tid + 1]);
   for (int w = tid; w < nwords; w += kTopkThreads) sh.bits[w] = wrow[w];
-  const int need = k_sel - st.sure;  // 0 <= need <= ncand (the row did not fail)
-  const int nc = st.ncand;
-  const uint2* cand = reinterpret_cast<const uint2*>(wrow + sel_words);
+  const SelectRowStats st = stats[row];
+  if (select_row_failed(st, n, k_sel)) return;  // select_fallback_kernel's row
+  const int need = k_sel - st.sure;  // 0 <= need <= ncand
+  if (need <= 0) c0 = c1 = 0;
+  const int p0 = (c0 + 1) & ~1, p1 = (c1 + 1) & ~1;  // padded: 16-byte copies
+  if (tid == 0) {
+    sh.neq = 0;
+    sh.abort = 0;
+    mbar_init(&sh.bar, 1);
+    fence_mbar_init();
+  }
+  // exclusive scan of the padded counts (nlists <= 2 * kTopkThreads)
+  static_assert(kFixLists <= 2 * kTopkThreads, "two lists per thread");
+  int incl = p0 + p1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) sh.warp_a[warp] = incl;
   __syncthreads();
-  if (need > 0 && need >= nc) {
-    for (int c = tid; c < nc; c += kTopkThreads) {
-      const uint32_t j = cand[c].y;
-      atomicOr(&sh.bits[j >> 5], 1u << (j & 31));
+  int before = incl - p0 - p1, total = 0;
+#pragma unroll
+  for (int w = 0; w < kTopkWarps; ++w) {
+    if (w < warp) before += sh.warp_a[w];
+    total += sh.warp_a[w];
+  }
+  if (need > 0) {
+    // one bulk copy per non-empty list, all in flight together
+    if (p0) bulk_load(&sh.cand[before], lists + static_cast<int64_t>(2 * tid) * cand_per_list,
+                      8u * p0, &sh.bar);
+    if (p1)
+      bulk_load(&sh.cand[before + p0], lists + static_cast<int64_t>(2 * tid + 1) * cand_per_list,
+                8u * p1, &sh.bar);
+    if (tid == 0) mbar_arrive_expect_tx(&sh.bar, 8u * total);
+    if (!mbar_wait(&sh.bar, 0, err, &sh.abort)) {
+      mbar_wait_drain(&sh.bar, 0, 200000000LL);  // copies in flight land before the CTA exits
+      return;
     }
+    // a list of odd length was copied with the slot after its last entry
+    if (p0 != c0) sh.cand[before + c0].y = kNoKey;
+    if (p1 != c1) sh.cand[before + p0 + c1].y = kNoKey;
+  }
+  __syncthreads();
+  auto set_bit = [&](int j) { atomicOr(&sh.bits[j >> 5], 1u << (j & 31)); };
+  if (need > 0 && need >= st.ncand) {
+    for (int e = tid; e < total; e += kTopkThreads)
+      if (sh.cand[e].y != kNoKey) set_bit(static_cast<int>(sh.cand[e].y));
   } else if (need > 0) {
-    // the need best candidates by (score desc, key asc): the need largest of
-    // the distinct 64-bit keys ord_key(score) << 32 | (2^32 - 1 - key), by an
-    // MSB-first radix select, 8 bits per pass
-    uint64_t* key = reinterpret_cast<uint64_t*>(sh.hist);
-    for (int c = tid; c < nc; c += kTopkThreads) {
-      const uint2 e = cand[c];
-      key[c] = (static_cast<uint64_t>(ord_key(__uint_as_float(e.x))) << 32) | (0xFFFFFFFFu - e.y);
-    }
-    uint64_t prefix = 0, pmask = 0;
-    int rem = need;
-    for (int shift = 56; shift >= 0; shift -= 8) {
-      for (int bn = tid; bn < 256; bn += kTopkThreads) rhist[bn] = 0;
+    // MSB-first radix select of the need-th largest key among the candidates,
+    // 9-bit digits of (key - ord_key(lo)) (all candidates lie in [lo, hi]):
+    // each level narrows to one digit value, until that bin is taken whole or
+    // holds a single key value (4 levels cover 32 bits); higher bins are
+    // taken, and the members of a single-value bin tie: the lowest columns win
+    uint32_t kmin = ord_key(st.lo), kmax = ord_key(st.hi);
+    if (kmin == kNegInfKey) kmin = 0u;          // an open bracket: the whole key range
+    if (kmax == 0xFF800000u) kmax = 0xFFFFFFFFu;
+    uint32_t lbase[kFixLevels];
+    int lsft[kFixLevels], lbin[kFixLevels], nlev = 0, rem = need;
+    lbase[0] = kmin;
+    lsft[0] = max(0, 32 - __clz(max(kmax - kmin, 1u)) - kFixDigit);
+    while (true) {
+      for (int bn = tid; bn < kFixBins; bn += kTopkThreads) sh.hist[bn] = 0;
       __syncthreads();
-      for (int c = tid; c < nc; c += kTopkThreads) {
-        const uint64_t K = key[c];
-        if ((K & pmask) == prefix) atomicAdd(&rhist[(K >> shift) & 255u], 1);
+      const int lv = nlev;
+      for (int e = tid; e < total; e += kTopkThreads) {
+        if (sh.cand[e].y == kNoKey) continue;
+        const uint32_t u = ord_key(__uint_as_float(sh.cand[e].x));
+        bool in = true;  // in the chosen bin of every level below lv
+#pragma unroll
+        for (int i = 0; i < kFixLevels; ++i)
+          if (i < lv) in = in && static_cast<int>((u - lbase[i]) >> lsft[i]) == lbin[i];
+        if (in) atomicAdd(&sh.hist[(u - lbase[lv]) >> lsft[lv]], 1);
       }
       __syncthreads();
-      find_digit256(sh, rhist, rem);
-      const int bin = sh.sh_bin;
+      find_threshold_bin<kFixBins>(sh, rem);
+      lbin[lv] = sh.sh_digit;
       rem -= sh.sh_above;
-      prefix |= static_cast<uint64_t>(sh.sh_digit) << shift;
-      pmask |= static_cast<uint64_t>(0xFFu) << shift;
-      __syncthreads();  // every thread has read sh_* before the next pass rewrites it
-      if (bin == rem) break;  // the rest of the class is taken whole
+      const int cnt = sh.sh_bin;
+      nlev = lv + 1;
+      if (cnt == rem || lsft[lv] == 0) break;  // the bin is the last
+      static_assert(kFixLevels * kFixDigit >= 32, "the last level's digit ends at bit 0");
+      lbase[nlev] = lbase[lv] + (static_cast<uint32_t>(lbin[lv]) << lsft[lv]);
+      lsft[nlev] = max(0, lsft[lv] - kFixDigit);
     }
-    for (int c = tid; c < nc; c += kTopkThreads) {
-      const uint64_t K = key[c];
-      if ((K & pmask) >= prefix) {
-        const uint32_t j = 0xFFFFFFFFu - static_cast<uint32_t>(K);
-        atomicOr(&sh.bits[j >> 5], 1u << (j & 31));
+    __syncthreads();  // every thread has read the last bin
+    const bool whole = sh.sh_bin == rem;  // the last bin is taken whole
+    for (int e = tid; e < total; e += kTopkThreads) {
+      const uint2 v = sh.cand[e];
+      if (v.y == kNoKey) continue;
+      const uint32_t u = ord_key(__uint_as_float(v.x));
+      int verdict = 0;  // 1 taken, -1 not, 0 member of the last bin
+#pragma unroll
+      for (int i = 0; i < kFixLevels; ++i) {
+        if (i < nlev && verdict == 0) {
+          const int bn = static_cast<int>((u - lbase[i]) >> lsft[i]);
+          verdict = bn > lbin[i] ? 1 : (bn < lbin[i] ? -1 : 0);
+        }
       }
+      if (verdict > 0 || (verdict == 0 && whole)) {
+        set_bit(static_cast<int>(v.y));
+      } else if (verdict == 0) {
+        sh.last[atomicAdd(&sh.neq, 1)] = static_cast<int>(v.y);  // <= ncand <= kFixCap
+      }
+    }
+    __syncthreads();
+    const int ne = whole ? 0 : sh.neq;
+    for (int e = tid; e < ne; e += kTopkThreads) {
+      const int j = sh.last[e];
+      int rank = 0;  // members with a lower column
+      for (int o = 0; o < ne; ++o) rank += sh.last[o] < j ? 1 : 0;
+      if (rank < rem) set_bit(j);
     }
   }
   __syncthreads();
   if (brow)
     for (int64_t w = tid; w < bm_words; w += kTopkThreads) brow[w] = w < nwords ? sh.bits[w] : 0u;
   if (irow || mrow) bits_to_lists(sh, nwords, irow, mrow);
+}
+
+// Rows whose bracket missed: the plain top-k of their full score rows (written
+// into the workspace by the indexer's kStoreFailed pass).  A fixed grid walks
+// the rows; CTAs skip rows that did not fail after reading their counters.
+template <int kGroups>
+__global__ void __launch_bounds__(kTopkThreads) select_fallback_kernel(
+    const float* __restrict__ ws, int64_t ws_stride, const SelectRowStats* __restrict__ stats,
+    int64_t rows, int Tq, int Tkv, int q_pos0, int k_sel, int32_t* __restrict__ indices,
+    uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask, int64_t bm_words) {
+  __shared__ TopkShared sh;
+  __shared__ int64_t failed[kTopkThreads];
+  __shared__ int nfailed;
+  // the CTA's rows, kTopkThreads at a time: each thread checks one, the failed
+  // ones are listed, then selected one after another by the whole CTA
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * kTopkThreads; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.x) * kTopkThreads) {
+    if (threadIdx.x == 0) nfailed = 0;
+    __syncthreads();
+    const int64_t row = r0 + threadIdx.x;
+    if (row < rows) {
+      const int n = min(q_pos0 + static_cast<int>(row % Tq) + 1, Tkv);
+      if (select_row_failed(stats[row], n, k_sel)) failed[atomicAdd(&nfailed, 1)] = row;
+    }
+    __syncthreads();
+    const int nf = nfailed;
+    for (int f = 0; f < nf; ++f) {
+      const int64_t fr = failed[f];
+      const int n = min(q_pos0 + static_cast<int>(fr % Tq) + 1, Tkv);
+      topk_row<true, kGroups>(sh, ws + fr * ws_stride, n, Tkv, k_sel, k_sel,
+                              indices ? indices + fr * k_sel : nullptr,
+                              mask ? mask + fr * k_sel : nullptr,
+                              bitmask ? bitmask + fr * bm_words : nullptr, bm_words);
+      __syncthreads();  // the next row reuses the shared memory
+    }
+  }
 }
 
 }  // namespace
@@ -997,25 +1154,45 @@ cudaError_t launch_select_threshold(const float* samples, int64_t stride, int B,
                                     SelectRowStats* stats, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * Tq;
   if (rows == 0) return cudaSuccess;
-  select_threshold_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-      samples, stride, Tq, Tkv, q_pos0, key_step, key_off, k_sel, z, stats);
+  select_threshold_kernel<<<static_cast<unsigned>((rows + kThrRows - 1) / kThrRows), kTopkThreads,
+                            0, stream>>>(samples, stride, rows, Tq, Tkv, q_pos0, key_step, key_off,
+                                         k_sel, z, stats);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select_scan(SelectRowStats* stats, int B, int Tq, int Tkv, int q_pos0,
+                               int k_sel, int tile_rows, cudaStream_t stream) {
+  const int64_t rows = static_cast<int64_t>(B) * Tq;
+  if (rows == 0) return cudaSuccess;
+  select_scan_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, stream>>>(
+      stats, rows, Tq, Tkv, q_pos0, k_sel, tile_rows);
   return cudaGetLastError();
 }
 
 cudaError_t launch_select_fixup(const uint32_t* ws, int64_t ws_stride, int64_t sel_words,
+                                int64_t cand_off, int cand_per_list, int keys_per_chunk,
                                 const SelectRowStats* stats, int B, int Tq, int Tkv, int q_pos0,
                                 int k_sel, int32_t* indices, uint8_t* mask, uint32_t* bitmask,
-                                int64_t bitmask_words, cudaStream_t stream) {
+                                int64_t bitmask_words, int* err, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(B) * Tq;
   if (rows == 0) return cudaSuccess;
-  auto kernel = Tkv >= kLongKeyRange ? select_fixup_kernel<kEmitLong>
-                                     : select_fixup_kernel<kEmitShort>;
-  kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
-      ws, ws_stride, sel_words, stats, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
-      bitmask_words);
+  select_fixup_kernel<<<static_cast<unsigned>(rows), kTopkThreads, 0, stream>>>(
+      ws, ws_stride, sel_words, cand_off, cand_per_list, keys_per_chunk, stats, Tq, Tkv, q_pos0,
+      k_sel, indices, mask, bitmask, bitmask_words, err);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // failed rows: a grid of a few CTAs per SM walks all rows
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = static_cast<unsigned>(
+      std::min<int64_t>((rows + kTopkThreads - 1) / kTopkThreads, 4LL * sms));
+  auto fb = Tkv >= kLongKeyRange ? select_fallback_kernel<kEmitLong>
+                                 : select_fallback_kernel<kEmitShort>;
+  fb<<<grid, kTopkThreads, 0, stream>>>(reinterpret_cast<const float*>(ws), ws_stride, stats,
+                                        rows, Tq, Tkv, q_pos0, k_sel, indices, mask, bitmask,
+                                        bitmask_words);
   return cudaGetLastError();
 }
-
-int select_fixup_capacity() { return kFixCap; }
 
 }  // namespace gsa

@@ -203,19 +203,29 @@ GSA_API int gsa_indexer_topk_adaptive(const void* q, int64_t q_stride,
  * expect for a key range of Tkv. */
 GSA_API int64_t gsa_bitmask_words(int Tkv);
 
-/* Bytes of caller-owned scratch that gsa_indexer_topk needs (the causal
- * score rows of the call: B * Tq rows of round-up-to-4(Tkv) floats). */
+/* Bytes of caller-owned scratch that gsa_indexer_topk needs: B * Tq rows of
+ * round-up-to-4(Tkv) floats (score rows, or a row's selection state) plus 32
+ * bytes of per-row counters. */
 GSA_API int64_t gsa_indexer_topk_workspace_size(int B, int Tq, int Tkv);
 
 /*
  * Indexer scores followed by top-k selection in one call: the forward's
  * GatedLightningIndexer.forward (gsa_ref.py:97-126) + AdaptiveTopKSelector
  * (gsa_ref.py:138-150), the pair the reference runs back to back at
- * gsa_ref.py:303-308 / gsa_opt.py:664-677.  The [B,Tq,Tkv] score rows exist
- * only in `workspace` (workspace_bytes >= gsa_indexer_topk_workspace_size);
- * only their causal part is written and read.  Arguments as for
+ * gsa_ref.py:303-308 / gsa_opt.py:664-677.  Arguments as for
  * gsa_indexer_scores and gsa_topk_select (any of indices / mask / bitmask
- * may be NULL).
+ * may be NULL); `workspace` holds workspace_bytes >=
+ * gsa_indexer_topk_workspace_size bytes of caller-owned scratch.
+ *
+ * The selection equals gsa_topk_select applied to gsa_indexer_scores' output,
+ * bit for bit.  With the fused selection (tensor-core path: bf16, H_I = 4,
+ * d_I = 64; see gsa_set_fused_selection) the score matrix is never written:
+ * each row's k-th score is bracketed from the row's scores against every 8th
+ * key, one pass over all keys sets the bits of the keys above the bracket and
+ * lists the few inside it, and a last pass ranks those exactly.  Rows whose
+ * bracket misses are recomputed in full and selected from their scores, so
+ * the result does not depend on the bracket.  Otherwise the causal score rows
+ * are written to the workspace and selected from there.
  */
 GSA_API int gsa_indexer_topk(const void* q, int64_t q_stride,
                              const void* k, int64_t k_stride,
@@ -226,8 +236,23 @@ GSA_API int gsa_indexer_topk(const void* q, int64_t q_stride,
                              int32_t* indices, uint8_t* mask,
                              uint32_t* bitmask, int64_t bitmask_words, void* stream);
 
-/* Size of the library's built-in scratch buffer for gsa_indexer_topk_noalloc. */
-#define GSA_NOALLOC_SCRATCH_BYTES (16ll << 20)
+/*
+ * Which selection gsa_indexer_topk (and gsa_indexer_topk_noalloc) uses on the
+ * tensor-core path, process-wide (no counterpart in the reference; a tuning
+ * and testing knob).  Both give the same bits.
+ *   GSA_FUSED_AUTO    the fused selection where it measured faster
+ *                     (Tkv >= 16 * k_sel), scores + top-k elsewhere (default)
+ *   GSA_FUSED_ALWAYS  the fused selection wherever it applies (Tkv > 2 * k_sel,
+ *                     Tkv <= 65536)
+ *   GSA_FUSED_NEVER   always scores + top-k
+ * Returns GSA_ERR_INVALID_ARG for another mode.
+ */
+typedef enum { GSA_FUSED_AUTO = 0, GSA_FUSED_ALWAYS = 1, GSA_FUSED_NEVER = 2 } gsa_fused_mode_t;
+GSA_API int gsa_set_fused_selection(int mode);
+
+/* Size of the library's built-in scratch buffer for gsa_indexer_topk_noalloc:
+ * gsa_indexer_topk_workspace_size(1, 2048, 2048), 16 MiB + 64 KiB. */
+#define GSA_NOALLOC_SCRATCH_BYTES ((16ll << 20) + (64ll << 10))
 
 /*
  * gsa_indexer_topk for callers that cannot allocate device memory.
@@ -239,21 +264,23 @@ GSA_API int gsa_indexer_topk(const void* q, int64_t q_stride,
  * and fragment the pool. Such callers cannot provide the scratch that
  * gsa_indexer_topk takes as `workspace`. This variant keeps that scratch
  * instead in a buffer compiled into the library: GSA_NOALLOC_SCRATCH_BYTES
- * (16 MiB) on every GPU that loads the library, held until the process exits.
+ * (16 MiB + 64 KiB) on every GPU that loads the library, held until the
+ * process exits.
  * The caller still passes all inputs and outputs. Arguments are those of
  * gsa_indexer_topk without workspace / workspace_bytes.
  *
  *   - Size limit: the call needs gsa_indexer_topk_workspace_size(B, Tq, Tkv)
- *     bytes (B * Tq rows of round-up-to-4(Tkv) floats; e.g. one 2048-token
- *     sequence).  Larger calls return GSA_ERR_UNSUPPORTED and say so in
- *     gsa_last_error_string(); use gsa_indexer_topk with a workspace then.
+ *     bytes (B * Tq rows of round-up-to-4(Tkv) floats plus 32 bytes each; up
+ *     to one 2048-token sequence).  Larger calls return GSA_ERR_UNSUPPORTED
+ *     and say so in gsa_last_error_string(); use gsa_indexer_topk with a
+ *     workspace then.
  *   - First call on a device: the first call of any gsa_* entry point on a
  *     device (this one included) looks up the device address of the buffer,
  *     once per device, with that device current.  Make that first call before
  *     any stream capture.  A device other than sm_100 gets GSA_ERR_NO_DEVICE.
  *   - Shared state: every call on a device uses the same buffer, which keeps
- *     the scores of the last call.  Nothing in it needs to start at zero,
- *     because each call writes every score it reads.  Calls whose work
+ *     the scratch of the last call.  Nothing in it needs to start at zero,
+ *     because each call writes every score, bit and counter it reads.  Calls whose work
  *     overlaps on the GPU (e.g. on two streams) race on the buffer; order
  *     them on one stream or use gsa_indexer_topk.
  *   - Allocation: no cudaMalloc, cudaFree or allocating library routine is

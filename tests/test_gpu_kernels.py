@@ -345,25 +345,63 @@ def test_gather_attention_vs_oracle(dtype):
 
 
 # ──────────────────────────────────────────────────────────── fused indexer + top-k
+@pytest.mark.parametrize("mode", [_lib.GSA_FUSED_AUTO, _lib.GSA_FUSED_ALWAYS, _lib.GSA_FUSED_NEVER])
 @pytest.mark.parametrize("B,Tq,Tkv,q_pos0,k_sel", [(2, 160, 160, 0, 48), (1, 700, 1500, 800, 256),
                                                    (1, 2048, 2048, 0, 2048),
-                                                   (1, 64, 40000, 39936, 2048)])  # long rows
-def test_indexer_topk_matches_separate_calls(B, Tq, Tkv, q_pos0, k_sel):
-    """The fused call (rows known finite) selects exactly as indexer + the standalone
-    selector (which also handles -inf), for short and for long (32K+ key) rows."""
+                                                   (1, 64, 40000, 39936, 2048),  # long rows
+                                                   (2, 256, 9000, 8744, 512)])
+def test_indexer_topk_matches_separate_calls(B, Tq, Tkv, q_pos0, k_sel, mode):
+    """gsa_indexer_topk (fused selection, or scores + top-k inside one call)
+    selects exactly as the indexer followed by the standalone selector (which
+    also handles -inf), for short and for long (32K+ key) rows."""
     q, k, w, bias = _indexer_inputs(B, Tq, Tkv, torch.bfloat16, seed=Tq)
     qc, kc, wc, bc = q.cuda(), k.cuda(), w.cuda(), bias.cuda()
     scores = ops.indexer_scores(qc, kc, wc, bc, 0.125, q_pos0=q_pos0, tkv=Tkv, fill_upper=False)
     i1, m1, b1 = ops.topk_select(scores, k_sel, q_pos0=q_pos0)
-    i2, m2, b2 = ops.indexer_topk(qc, kc, wc, bc, 0.125, k_sel, q_pos0=q_pos0, tkv=Tkv,
-                                  want_indices=True, want_mask=True, want_bitmask=True)
+    with _lib.fused_selection(mode):
+        i2, m2, b2 = ops.indexer_topk(qc, kc, wc, bc, 0.125, k_sel, q_pos0=q_pos0, tkv=Tkv,
+                                      want_indices=True, want_mask=True, want_bitmask=True)
     assert torch.equal(i1, i2) and torch.equal(m1, m2) and torch.equal(b1, b2)
+
+
+def test_set_fused_selection_rejects_unknown_mode():
+    lib = _lib.load()
+    assert lib.gsa_set_fused_selection(7) == 1
+    assert lib.gsa_set_fused_selection(_lib.GSA_FUSED_AUTO) == 0
+
+
+@pytest.mark.parametrize("pattern", ["ties", "periodic", "mixed"])
+def test_indexer_topk_rows_whose_bracket_misses(pattern):
+    """Inputs that defeat the fused selection's sampled bracket of the k-th
+    score (forced on for this size) still select exactly as the split calls:
+    * ties: q = 0, so every key of a row scores the same (the candidate lists
+      overflow; the lowest k columns win);
+    * periodic: keys at positions 7 mod 8 (the sampled ones) score far lower
+      than the rest, so the samples misjudge every row's k-th score;
+    * mixed: ties in even rows only, so failed and clean rows share row blocks."""
+    B, Tq, Tkv, q_pos0, k_sel = 1, 300, 3000, 2700, 256
+    q, k, w, bias = _indexer_inputs(B, Tq, Tkv, torch.bfloat16, seed=21)
+    if pattern in ("ties", "mixed"):
+        rows = slice(None) if pattern == "ties" else slice(0, None, 2)
+        q[:, rows] = 0
+    if pattern == "periodic":
+        k[:, 7::8] = -k[:, 7::8].abs() * 4
+        q = q.abs()
+    qc, kc, wc, bc = q.cuda(), k.cuda(), w.cuda(), bias.cuda()
+    scores = ops.indexer_scores(qc, kc, wc, bc, 0.125, q_pos0=q_pos0, tkv=Tkv, fill_upper=False)
+    i1, m1, b1 = ops.topk_select(scores, k_sel, q_pos0=q_pos0)
+    with _lib.fused_selection(_lib.GSA_FUSED_ALWAYS):
+        i2, m2, b2 = ops.indexer_topk(qc, kc, wc, bc, 0.125, k_sel, q_pos0=q_pos0, tkv=Tkv,
+                                      want_indices=True, want_mask=True, want_bitmask=True)
+    assert torch.equal(i1, i2) and torch.equal(m1, m2) and torch.equal(b1, b2)
+    if pattern == "ties":  # all tied: the lowest k_sel columns of every row
+        assert torch.equal(i2[0].cpu(), torch.arange(k_sel, dtype=torch.int32).expand(Tq, k_sel))
 
 
 def test_indexer_topk_rejects_small_workspace():
     lib = _lib.load()
     need = lib.gsa_indexer_topk_workspace_size(1, 100, 100)
-    assert need == 100 * 100 * 4
+    assert need == 100 * (100 * 4 + 32)
     rc = lib.gsa_indexer_topk(None, 256, None, 64, None, 4, None, 0.125, 0, 1, 100, 100, 0, 4, 64,
                               16, 4096, need - 4, None, None, None, 4, None)
     assert rc == 1

@@ -4,8 +4,8 @@ Some callers cannot call cudaMalloc: a plugin running inside a host engine
 that owns all device memory, or a runtime that fixes its memory budget at
 start-up (an allocation can synchronise the device and fragment the pool).
 They cannot pass gsa_indexer_topk the scratch it takes as `workspace`, so
-this variant keeps that scratch in a buffer built into the library (16 MiB per
-GPU).  The test calls it through the C ABI and checks:
+this variant keeps that scratch in a buffer built into the library (16 MiB +
+64 KiB per GPU).  The test calls it through the C ABI and checks:
 
 * its outputs against gsa_indexer_topk with a caller workspace, on calls in a
   row whose shapes differ, so the scores one call leaves in the shared buffer
@@ -15,8 +15,8 @@ GPU).  The test calls it through the C ABI and checks:
 * its selections against the CPU oracle's scores under the (score desc, index
   asc) rule, modulo keys within 1e-4 (relative) of the k-th score (the
   tensor-core scores are ~1e-5 from the oracle's);
-* the exact size limit: B=1, Tq=Tkv=2048 needs exactly the 16 MiB built in and
-  is accepted, a larger call is refused with a clear message;
+* the exact size limit: B=1, Tq=Tkv=2048 needs exactly the 16 MiB + 64 KiB
+  built in and is accepted, a larger call is refused with a clear message;
 * that the calls take no device memory: the driver's free-memory figure
   (cudaMemGetInfo) is the same before and after them (the first call, which
   loads the library's kernels onto the device, comes before the measurement).
@@ -34,7 +34,7 @@ pytestmark = pytest.mark.gpu
 torch.set_grad_enabled(False)
 
 GSA_ERR_UNSUPPORTED = 3
-SCRATCH_BYTES = 16 << 20
+SCRATCH_BYTES = (16 << 20) + (64 << 10)
 
 
 def _inputs(B, Tq, Tkv, seed):
@@ -92,13 +92,21 @@ def _check_vs_oracle(cpu_in, Tkv, q_pos0, k_sel, idx, msk):
 CASES = [  # B, Tq, Tkv, q_pos0, k_sel, seed
     (1, 700, 1500, 800, 256, 11),
     (2, 160, 160, 0, 48, 12),
-    (1, 2048, 2048, 0, 256, 14),  # exactly the 16 MiB built in
+    (1, 2048, 2048, 0, 256, 14),  # exactly the buffer built in
 ]
 
 
-def test_noalloc_matches_workspace_entry_and_oracle_on_calls_in_a_row():
+@pytest.mark.parametrize("mode", [_lib.GSA_FUSED_AUTO, _lib.GSA_FUSED_ALWAYS])
+def test_noalloc_matches_workspace_entry_and_oracle_on_calls_in_a_row(mode):
+    """With the automatic selection (scores + top-k at these sizes) and with
+    the fused selection forced on."""
     build()
     lib = _lib.load()
+    with _lib.fused_selection(mode):
+        _noalloc_calls_in_a_row(lib)
+
+
+def _noalloc_calls_in_a_row(lib):
     assert lib.gsa_indexer_topk_workspace_size(1, 2048, 2048) == SCRATCH_BYTES
     prepared = []
     for B, Tq, Tkv, q_pos0, k_sel, seed in CASES:
@@ -133,7 +141,7 @@ def test_noalloc_matches_workspace_entry_and_oracle_on_calls_in_a_row():
 def test_noalloc_refuses_calls_beyond_its_buffer():
     build()
     lib = _lib.load()
-    B, Tq, Tkv = 1, 2049, 2048  # one row more than the 16 MiB built in
+    B, Tq, Tkv = 1, 2049, 2048  # one row more than the buffer built in
     assert lib.gsa_indexer_topk_workspace_size(B, Tq, Tkv) > SCRATCH_BYTES
     q, k, w, bias = (t.cuda() for t in _inputs(B, Tq, Tkv, 13))
     words = lib.gsa_bitmask_words(Tkv)
