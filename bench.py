@@ -53,7 +53,7 @@ UNIT = "tokens/s"
 # N=1, per configuration, each from an ncu capture of that configuration's
 # bench command (the algorithmic bytes of a launch, for comparison: q, k, v, og
 # and out read/written once plus the bitmask, B*T*(5*D*2 + 4*ceil(T/128)*4)).
-ATTN_TRAFFIC_BYTES_PER_LAUNCH = {"cfg3": 363_120_000}
+ATTN_TRAFFIC_BYTES_PER_LAUNCH = {"cfg2": 71_964_672, "cfg3": 363_120_000, "cfg4": 1_379_490_560}
 
 
 def workload_string(cfg) -> str:

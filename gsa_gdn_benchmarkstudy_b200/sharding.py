@@ -63,6 +63,45 @@ def all_gather_equal(t: torch.Tensor, group) -> torch.Tensor:
     return out
 
 
+def all_gather_async(out: torch.Tensor, t: torch.Tensor, group):
+    """Start an all-gather of equally shaped ``t`` into ``out`` [world, *t.shape]
+    (contiguous); returns the work handle (NCCL or gloo)."""
+    t = t.contiguous()
+    if dist.get_backend(group) == "nccl":
+        return dist.all_gather_into_tensor(out, t, group=group, async_op=True)
+    return dist.all_gather(list(out.unbind(0)), t, group=group, async_op=True)
+
+
+class RowBlockGather:
+    """The full [1, T, W] output from every rank's two zig-zag row blocks,
+    gathered one block at a time so that a block's all-gather overlaps the
+    work that follows it.
+
+    Rank r's first block is sequence block r, so the ranks' first blocks
+    gathered rank-major are sequence blocks 0..P-1 and land in place; rank r's
+    second block is sequence block 2P-1-r, so the second gather comes in
+    reverse order and is copied into place once it has arrived."""
+
+    def __init__(self, T: int, world: int, width: int, dtype, device):
+        self.world, self.n = world, T // (2 * world)
+        self.out = torch.empty(1, T, width, dtype=dtype, device=device)
+        self.late = torch.empty(world, self.n, width, dtype=dtype, device=device)
+        self.works = []
+
+    def add(self, i: int, block: torch.Tensor, group) -> None:
+        """Start gathering this rank's block ``i`` (0 or 1), [n, W]."""
+        P, n = self.world, self.n
+        target = self.out[0, :P * n].view(P, n, -1) if i == 0 else self.late
+        self.works.append(all_gather_async(target, block, group))
+
+    def finish(self) -> torch.Tensor:
+        for w in self.works:
+            w.wait()
+        P, n = self.world, self.n
+        self.out[0, P * n:].copy_(self.late.flip(0).reshape(P * n, -1))
+        return self.out
+
+
 def zigzag_order(T: int, world: int, device) -> torch.Tensor:
     """For each sequence row, its row in the rank-major all-gather of zig-zag shards."""
     src = torch.empty(T, dtype=torch.long)
@@ -185,13 +224,22 @@ class ShardedGSA:
         m = self.model
         with _Stage(m, "lib:proj_gemm", "gsa_b200/fused_proj"):
             proj = m.project(x_loc)
-        outs = self._rows_from_projection(proj, x_loc.dtype)
-        with _Stage(m, "lib:o_proj", "gsa_b200/o_proj"):
-            out_local = F.linear(torch.cat(outs, dim=1), m.o_proj.weight)
         if not gather:
-            return out_local
-        with _Stage(m, "comm:out_allgather", "gsa_b200/out_allgather"):
-            return gather_rows(out_local, self.T, self.group, self._row_order(x_loc.device))
+            outs = self._rows_from_projection(proj, x_loc.dtype)
+            with _Stage(m, "lib:o_proj", "gsa_b200/o_proj"):
+                return F.linear(torch.cat(outs, dim=1), m.o_proj.weight)
+        # o_proj and the output all-gather per block: the first (early, light)
+        # block's gather runs while the second block computes
+        gat = RowBlockGather(self.T, self.world, m.hidden_size, x_loc.dtype, x_loc.device)
+
+        def block_out(i, o, n, a):
+            with _Stage(m, "lib:o_proj", "gsa_b200/o_proj"):
+                y = F.linear(a[0], m.o_proj.weight)
+            gat.add(i, y, self.kv_group)
+
+        self._rows_from_projection(proj, x_loc.dtype, per_block=block_out)
+        with _Stage(m, "comm:out_allgather_wait", "gsa_b200/out_allgather"):
+            return gat.finish()
 
     def _rows_from_projection(self, proj: torch.Tensor, dtype, per_block=None) -> list:
         """Everything after the projection GEMM of this rank's rows: gathers,
@@ -204,9 +252,11 @@ class ShardedGSA:
         dev = proj.device
         order = self._row_order(dev)
         parts = m.split(proj)
-        # the selection needs only the indexer keys of the whole sequence (2 MB at T=16K)
-        with _Stage(m, "comm:ik_allgather", "gsa_b200/ik_allgather"):
-            ik_full = gather_rows(parts["ik"].contiguous(), T, self.group, order)
+        # the selection needs only the indexer keys of the whole sequence (2 MB at
+        # T=16K): gathered while RoPE runs
+        ik_loc = parts["ik"][0]
+        g_ik = torch.empty((self.world, *ik_loc.shape), dtype=ik_loc.dtype, device=dev)
+        w_ik = all_gather_async(g_ik, ik_loc, self.group)
         cos, sin = m.rotary_emb(T, dev, dtype)
         pos = self._positions(dev)
         with _Stage(m, "k:rope_gates", "gsa_b200/rope_gates"):
@@ -224,6 +274,9 @@ class ShardedGSA:
                                  async_op=True)
             wv = dist.all_gather(list(gv.unbind(0)), v[0].contiguous(), group=self.kv_group,
                                  async_op=True)
+        with _Stage(m, "comm:ik_allgather_wait", "gsa_b200/ik_allgather"):
+            w_ik.wait()
+            ik_full = unshard_rows(g_ik, order)
         blocks, off = [], 0
         for s, e in self.blocks:
             n = e - s

@@ -8,8 +8,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from gsa_gdn_benchmarkstudy_b200.sharding import (causal_row_cost, gather_batch, gather_rows,
-                                                  unshard_rows, zigzag_blocks, zigzag_order)
+from gsa_gdn_benchmarkstudy_b200.sharding import (RowBlockGather, causal_row_cost, gather_batch,
+                                                  gather_rows, unshard_rows, zigzag_blocks,
+                                                  zigzag_order)
 
 
 @pytest.mark.parametrize("T,world", [(16384, 1), (16384, 2), (16384, 8), (65536, 8), (64, 4)])
@@ -65,6 +66,11 @@ def _worker(rank, world, port, T, q):
         local = torch.cat([full[:, s:e] for s, e in zigzag_blocks(T, world, rank)], dim=1)
         got = gather_rows(local, T, dist.group.WORLD)
         ok_rows = torch.equal(got, full)
+        # the per-block form the sharded forward uses: block 0 gathered first
+        gat = RowBlockGather(T, world, 3, torch.float32, torch.device("cpu"))
+        for i, (s, e) in enumerate(zigzag_blocks(T, world, rank)):
+            gat.add(i, full[0, s:e], dist.group.WORLD)
+        ok_rows = ok_rows and torch.equal(gat.finish(), full)
         xb = torch.arange(4 * 5 * 2, dtype=torch.float32).view(4, 5, 2)
         per = 4 // world
         gb = gather_batch(xb[rank * per:(rank + 1) * per], dist.group.WORLD)
