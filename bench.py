@@ -519,9 +519,66 @@ def run_ours(args, cfg, rank: int, world: int, device):
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_sample_rows, os.cpu_count() or 1)
-    if world == 1 and args.gpu_reference:
-        line["gpu_reference"] = gpu_reference(cfg, device)
+    if world == 1:
+        ref_mod = None
+        if args.gpu_reference:
+            line["gpu_reference"] = gpu_reference(cfg, device)
+            ref_mod = sys.modules.get("gsa_opt")
+        line["gather_attention"] = time_gather_attention(device, reference=ref_mod)
     print(json.dumps(line), flush=True)
+
+
+def time_gather_attention(device, name: str = "cfg2", iters: int = 3, reference=None) -> dict:
+    """The index-gather attention kernel (the op-level fused_sparse_attention /
+    sparse_attention_ref, gsa_opt.py:349-383) on a configuration's own q, k, v
+    and top-k index lists, event-timed.  Its work is the gathered K and V rows
+    of every selected (query, key) pair plus q in, out and the indices
+    (WorkModel.attn_gather_bytes), reported as GB/s and as a fraction of the
+    measured HBM peak; the rows mostly come from L2.  With ``reference`` (the
+    gsa_opt module) the reference's Triton kernel is timed on the same inputs."""
+    from gsa_gdn_benchmarkstudy_b200 import ops
+    from gsa_gdn_benchmarkstudy_b200.workloads import CONFIGS, WorkModel, make_input
+
+    c = CONFIGS[name]
+    m = build_model(c, device)
+    x = make_input(c, device=device)
+    parts = m.split(m.project(x))
+    cos, sin = m.rotary_emb(c.T, device, x.dtype)
+    q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, c.H, v_src=parts["v"],
+                             vg_src=parts["vg"])
+    ix = m.indexer
+    idx, mask, _ = ops.indexer_topk(parts["iq"], parts["ik"], parts["iw"], ix.bias_f32(),
+                                    ix.scale, c.k_eff, want_indices=True, want_mask=True,
+                                    want_bitmask=False)
+    shape = (c.B, c.T, c.H, c.d_head)
+    q4, k4, v4 = q.view(shape), k.view(shape), v.view(shape)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    ms = timed(lambda: ops.fused_sparse_attention(q4, k4, v4, idx, mask, m.scale))
+    gb = WorkModel(c).attn_gather_bytes / 1e9
+    res = {"workload": workload_string(c), "kernel": "gather_attn_kernel", "ms": round(ms, 3),
+           "gathered_gbs": round(gb / (ms / 1e3), 1),
+           "frac_of_hbm": round(gb / (ms / 1e3) / peaks()["hbm_gbs"], 4)}
+    if reference is not None:
+        try:
+            idx64 = idx.long()
+            rms = timed(lambda: reference.fused_sparse_attention(q4, k4, v4, idx64, mask, m.scale))
+            res["reference_triton_ms"] = round(rms, 3)
+        except Exception as exc:  # the reference kernel failed to compile or run
+            res["reference_triton_error"] = f"{type(exc).__name__}: {exc}"[:200]
+    del m
+    torch.cuda.empty_cache()
+    return res
 
 
 def time_indexer_and_topk(model, x, cfg, iters: int = 5):

@@ -10,9 +10,14 @@
 // without loading their K/V rows, and duplicate indices count once per slot
 // exactly as in the reference.
 //
-// One warp per (b, t, h): every lane owns d/32 consecutive channels; each
-// warp reads 32 (index, mask) pairs with one coalesced load and broadcasts
-// them by shuffle; K and V rows are read with vector loads.
+// One warp per (b, t, h): every lane owns d/32 consecutive channels.  A warp
+// reads 32 (index, mask) pairs with one coalesced load, then works through
+// the live slots eight at a time: the eight K and V row slices of a group are
+// loaded together (sixteen independent vector loads per lane in flight, the
+// rows mostly come from L2), the eight dot products are reduced across the
+// warp together, and the online softmax takes the group in one step.  The
+// kernel is bound by the L2/DRAM traffic of the gathered rows, 2 * d * sizeof
+// per live slot and head.
 #include "kernels.h"
 
 namespace gsa {
@@ -66,6 +71,39 @@ struct Lanes<float, D> {
   }
 };
 
+// A lane's N channels of one K or V row, kept as loaded (bf16 pairs or fp32)
+// until they are used: half the registers of a float copy for bf16.
+template <typename E, int N>
+struct Raw {
+  static constexpr int kWords = N * static_cast<int>(sizeof(E)) / 4;
+  uint32_t w[kWords];
+  __device__ __forceinline__ void load(const E* p) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p);
+    if constexpr (kWords % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < kWords; i += 4) {
+        const uint4 t = reinterpret_cast<const uint4*>(src)[i / 4];
+        w[i] = t.x; w[i + 1] = t.y; w[i + 2] = t.z; w[i + 3] = t.w;
+      }
+    } else if constexpr (kWords == 2) {
+      const uint2 t = *reinterpret_cast<const uint2*>(src);
+      w[0] = t.x; w[1] = t.y;
+    } else {
+      w[0] = src[0];
+    }
+  }
+  __device__ __forceinline__ float get(int e) const {
+    if constexpr (sizeof(E) == 2) {
+      const uint32_t x = w[e >> 1];
+      return __uint_as_float((e & 1) ? (x & 0xFFFF0000u) : (x << 16));
+    } else {
+      return __uint_as_float(w[e]);
+    }
+  }
+};
+
+constexpr int kGroup = 8;  // live slots per step
+
 template <typename E, int D>
 __global__ void __launch_bounds__(256) gather_attn_kernel(
     const E* __restrict__ q, int64_t q_stride, const E* __restrict__ k, int64_t k_stride,
@@ -103,24 +141,59 @@ __global__ void __launch_bounds__(256) gather_attn_kernel(
     }
     uint32_t live = __ballot_sync(0xFFFFFFFFu, vl);
     while (live) {
-      const int src = __ffs(live) - 1;
-      live &= live - 1;
-      const int j = __shfl_sync(0xFFFFFFFFu, jl, src);
-      float kv[N], vv[N];
-      L::load(kb + static_cast<int64_t>(j) * k_stride, kv);
-      L::load(vb + static_cast<int64_t>(j) * v_stride, vv);
-      float part = 0.f;
+      // the next (up to) kGroup live slots of this window
+      int j[kGroup];
+      int cnt = 0;
 #pragma unroll
-      for (int e = 0; e < N; ++e) part = fmaf(qv[e], kv[e], part);
+      for (int u = 0; u < kGroup; ++u) {
+        const int src = live ? __ffs(live) - 1 : 0;
+        j[u] = __shfl_sync(0xFFFFFFFFu, jl, src);
+        cnt += live ? 1 : 0;
+        live &= live - 1;
+      }
+      Raw<E, N> kv[kGroup], vv[kGroup];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
-      const float sc = part * scale;
-      const float m_new = fmaxf(m, sc);
-      const float alpha = expf(m - m_new);  // 0 on the first live slot (m = -inf)
-      const float p = expf(sc - m_new);
-      l = l * alpha + p;
+      for (int u = 0; u < kGroup; ++u) {
+        if (u < cnt) {
+          kv[u].load(kb + static_cast<int64_t>(j[u]) * k_stride);
+          vv[u].load(vb + static_cast<int64_t>(j[u]) * v_stride);
+        }
+      }
+      float sc[kGroup];
 #pragma unroll
-      for (int e = 0; e < N; ++e) acc[e] = fmaf(p, vv[e], acc[e] * alpha);
+      for (int u = 0; u < kGroup; ++u) {
+        float part = 0.f;
+        if (u < cnt) {
+#pragma unroll
+          for (int e = 0; e < N; ++e) part = fmaf(qv[e], kv[u].get(e), part);
+        }
+        sc[u] = part;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int u = 0; u < kGroup; ++u) sc[u] += __shfl_xor_sync(0xFFFFFFFFu, sc[u], o);
+      }
+      float gmax = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kGroup; ++u) {
+        sc[u] = u < cnt ? sc[u] * scale : -INFINITY;
+        gmax = fmaxf(gmax, sc[u]);
+      }
+      const float m_new = fmaxf(m, gmax);
+      const float alpha = expf(m - m_new);  // 0 on the first live group (m = -inf)
+      l *= alpha;
+#pragma unroll
+      for (int e = 0; e < N; ++e) acc[e] *= alpha;
+#pragma unroll
+      for (int u = 0; u < kGroup; ++u) {
+        if (u < cnt) {
+          const float p = expf(sc[u] - m_new);
+          l += p;
+#pragma unroll
+          for (int e = 0; e < N; ++e) acc[e] = fmaf(p, vv[u].get(e), acc[e]);
+        }
+      }
       m = m_new;
     }
   }
