@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-rows", type=int, default=256)
+    ap.add_argument("--unfused-projection", action="store_true",
+                    help="cuBLAS addmm + the separate RoPE/gate kernel instead of the "
+                         "projection GEMM with RoPE and the value gate in its epilogue")
     ap.add_argument("--adaptive-k", action="store_true",
                     help="opt-in variance-based k per row (not the reference module's fixed k)")
     ap.add_argument("--gpu-reference", action="store_true",
@@ -342,6 +345,7 @@ def run_ours(args, cfg, rank: int, world: int, device):
     _lib.load()
     torch.set_grad_enabled(False)
     model = build_model(cfg, device, args.adaptive_k)
+    model.use_fused_epilogue = not args.unfused_projection
     x_host = make_input(cfg).pin_memory()
 
     if world > 1:

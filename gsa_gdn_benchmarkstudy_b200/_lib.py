@@ -81,6 +81,17 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp],
     ),
+    "gsa_fused_projection": (
+        _i32,
+        [_vp, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _i64,
+         _vp, _vp, _vp, _vp, _i64, _vp],
+    ),
+    "gsa_fused_projection_rows": (_i64, [_i32, _i32, _i32]),
+    "gsa_fused_projection_rest_width": (_i64, [_i32, _i32, _i32]),
+    "gsa_fused_projection_pack": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp],
+    ),
 }
 
 _lock = threading.Lock()

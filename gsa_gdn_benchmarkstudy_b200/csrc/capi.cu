@@ -128,6 +128,43 @@ int make_map_bf16_3d(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
   return GSA_OK;
 }
 
+// 2-D bf16 map over [rows][cols] with row stride `row_bytes`; box {64,
+// box_rows} with 128-byte swizzle; loads fill zeros out of bounds, stores
+// are clipped there.
+int make_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                     uint64_t row_bytes, uint32_t box_rows) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (!fn) return set_error(GSA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled failed (%d)",
+                  static_cast<int>(r));
+    return GSA_ERR_CUDA;
+  }
+  return GSA_OK;
+}
+
+// Layout of the packed projection weight of gsa_fused_projection (the tile
+// order proj_gemm.cu documents): q and k in D/256 tiles each, v/vg
+// interleaved in D/128 tiles, then og | iq | ik | iw | zeros.
+struct ProjLayout {
+  int D, H_I, d_I;
+  int64_t rest_cols() const { return D + static_cast<int64_t>(H_I) * d_I + d_I + H_I; }
+  int q_tiles() const { return D / 256; }
+  int v_tiles() const { return D / 128; }
+  int rest_tiles() const { return static_cast<int>((rest_cols() + 255) / 256); }
+  int n_tiles() const { return 2 * q_tiles() + v_tiles() + rest_tiles(); }
+  int64_t rows() const { return static_cast<int64_t>(n_tiles()) * 256; }
+  int64_t rest_width() const { return (rest_cols() + 63) / 64 * 64; }
+  bool ok() const { return D > 0 && D % 256 == 0 && H_I > 0 && d_I > 0; }
+};
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int finish(cudaError_t e) { return e == cudaSuccess ? GSA_OK : set_cuda_error(e); }
@@ -733,6 +770,120 @@ int gsa_output_gate(const void* o, int64_t o_stride, const void* og, int64_t og_
   if (rc) return rc;
   return finish(gsa::launch_output_gate(o, o_stride, og, og_stride, out, out_stride, dtype, rows,
                                         width, static_cast<cudaStream_t>(stream)));
+}
+
+int64_t gsa_fused_projection_rows(int D, int H_I, int d_I) {
+  const ProjLayout L{D, H_I, d_I};
+  return L.ok() ? L.rows() : 0;
+}
+
+int64_t gsa_fused_projection_rest_width(int D, int H_I, int d_I) {
+  const ProjLayout L{D, H_I, d_I};
+  return L.ok() ? L.rest_width() : 0;
+}
+
+int gsa_fused_projection_pack(const void* w_q, const void* w_k, const void* w_v, const void* w_vg,
+                              const void* w_og, const void* w_iq, const void* w_ik,
+                              const void* w_iw, const float* b_vg, const float* b_og,
+                              const float* b_iw, int D, int H_I, int d_I, void* w_packed,
+                              float* b_packed, void* stream) {
+  const ProjLayout L{D, H_I, d_I};
+  if (!L.ok())
+    return set_error(GSA_ERR_UNSUPPORTED, "D must be a positive multiple of 256, H_I, d_I > 0");
+  if (!w_q || !w_k || !w_v || !w_vg || !w_og || !w_iq || !w_ik || !w_iw || !w_packed || !b_packed)
+    return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t row = static_cast<size_t>(D) * 2;
+  char* wp = static_cast<char*>(w_packed);
+  cudaError_t e = cudaSuccess;
+  auto rows_to = [&](int64_t dst_row, const void* src, int64_t src_row, int64_t n) {
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(wp + dst_row * row, static_cast<const char*>(src) + src_row * row,
+                          n * row, cudaMemcpyDeviceToDevice, s);
+  };
+  auto bias_to = [&](int64_t dst, const float* src, int64_t src_off, int64_t n) {
+    if (e == cudaSuccess && src)
+      e = cudaMemcpyAsync(b_packed + dst, src + src_off, n * sizeof(float),
+                          cudaMemcpyDeviceToDevice, s);
+  };
+  rows_to(0, w_q, 0, D);
+  rows_to(D, w_k, 0, D);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b_packed, 0, L.rows() * sizeof(float), s);
+  for (int i = 0; i < D / 128; ++i) {
+    const int64_t t0 = 2 * static_cast<int64_t>(D) + 256 * i;
+    rows_to(t0, w_v, 128 * i, 128);
+    rows_to(t0 + 128, w_vg, 128 * i, 128);
+    bias_to(t0 + 128, b_vg, 128 * i, 128);
+  }
+  int64_t r = 4 * static_cast<int64_t>(D);
+  rows_to(r, w_og, 0, D);
+  bias_to(r, b_og, 0, D);
+  r += D;
+  rows_to(r, w_iq, 0, static_cast<int64_t>(H_I) * d_I);
+  r += static_cast<int64_t>(H_I) * d_I;
+  rows_to(r, w_ik, 0, d_I);
+  r += d_I;
+  rows_to(r, w_iw, 0, H_I);
+  bias_to(r, b_iw, 0, H_I);
+  r += H_I;
+  if (e == cudaSuccess) e = cudaMemsetAsync(wp + r * row, 0, (L.rows() - r) * row, s);
+  return finish(e);
+}
+
+int gsa_fused_projection(const void* x, int64_t x_stride, const void* w_packed,
+                         const float* b_packed, int M, int D, int H, int d, int H_I, int d_I,
+                         int T, int pos0, const void* cos, const void* sin, int64_t table_rows,
+                         void* q_out, void* k_out, void* v_out, void* rest, int64_t rest_stride,
+                         void* stream) {
+  const ProjLayout L{D, H_I, d_I};
+  if (M < 0 || H <= 0 || d <= 0 || T <= 0 || pos0 < 0 || table_rows < 0)
+    return set_error(GSA_ERR_INVALID_ARG, "bad sizes");
+  if (d != 128 || static_cast<int64_t>(H) * d != D || !L.ok())
+    return set_error(GSA_ERR_UNSUPPORTED, "needs d == 128, D == H*d, D a multiple of 256");
+  if (M == 0) return GSA_OK;
+  if (!x || !w_packed || !b_packed || !cos || !sin || !q_out || !k_out || !v_out || !rest)
+    return set_error(GSA_ERR_INVALID_ARG, "null pointer");
+  if (x_stride < D || rest_stride < L.rest_width())
+    return set_error(GSA_ERR_INVALID_ARG, "x_stride < D or rest_stride < the rest width");
+  if (table_rows < static_cast<int64_t>(pos0) + std::min(T, M))
+    return set_error(GSA_ERR_INVALID_ARG, "rotary tables end before the last position");
+  if (!aligned16(x) || (x_stride * 2) % 16 || !aligned16(w_packed) || !aligned16(b_packed) ||
+      !aligned16(cos) || !aligned16(sin) || !aligned16(q_out) || !aligned16(k_out) ||
+      !aligned16(v_out) || !aligned16(rest) || (rest_stride * 2) % 16)
+    return set_error(GSA_ERR_ALIGNMENT, "rows must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int clusters = gsa::proj_gemm_max_clusters();
+  if (clusters <= 0) return set_error(GSA_ERR_CUDA, "no two-CTA cluster fits this device");
+  CUtensorMap xmap, wmap, qmap, kmap, vmap, rmap;
+  if ((rc = make_map_bf16_2d(&xmap, x, D, M, x_stride * 2, 128))) return rc;
+  if ((rc = make_map_bf16_2d(&wmap, w_packed, D, L.rows(), static_cast<uint64_t>(D) * 2, 128)))
+    return rc;
+  if ((rc = make_map_bf16_2d(&qmap, q_out, D, M, static_cast<uint64_t>(D) * 2, 32))) return rc;
+  if ((rc = make_map_bf16_2d(&kmap, k_out, D, M, static_cast<uint64_t>(D) * 2, 32))) return rc;
+  if ((rc = make_map_bf16_2d(&vmap, v_out, D, M, static_cast<uint64_t>(D) * 2, 32))) return rc;
+  if ((rc = make_map_bf16_2d(&rmap, rest, L.rest_width(), M, rest_stride * 2, 32))) return rc;
+  gsa::ProjGemmArgs a{};
+  a.M = M;
+  a.K = D;
+  a.n_tiles = L.n_tiles();
+  a.q_tiles = L.q_tiles();
+  a.v_tiles = L.v_tiles();
+  a.rest_boxes = static_cast<int>(L.rest_width() / 64);
+  a.T = T;
+  a.pos0 = pos0;
+  a.cos = static_cast<const __nv_bfloat16*>(cos);
+  a.sin = static_cast<const __nv_bfloat16*>(sin);
+  a.bias = b_packed;
+  a.err = st->err;
+  const int64_t tiles = (static_cast<int64_t>(M) + 255) / 256 * L.n_tiles();
+  clusters = static_cast<int>(std::min<int64_t>(clusters, tiles));
+  return finish(gsa::launch_proj_gemm(xmap, wmap, qmap, kmap, vmap, rmap, a, clusters,
+                                      static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

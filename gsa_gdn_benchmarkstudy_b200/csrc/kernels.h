@@ -164,6 +164,32 @@ cudaError_t launch_masked_attention(const CUtensorMap& qmap, const CUtensorMap& 
                                     const CUtensorMap& vmap, const MaskedAttnArgs& a,
                                     cudaStream_t stream);
 
+// Fused projection GEMM (proj_gemm.cu): x [M, K] times the packed weight
+// [n_tiles * 256, K] (both bf16, K-major), with RoPE on the q and k column
+// tiles, the value gate on the v/vg tiles and the bias on the rest tiles.
+struct ProjGemmArgs {
+  int M;           // rows of x
+  int K;           // reduction width (hidden size), a multiple of 64
+  int n_tiles;     // 256-column tiles of the packed weight
+  int q_tiles;     // tiles of q (and of k): hidden / 256
+  int v_tiles;     // v/vg tiles: hidden / 128
+  int rest_boxes;  // 64-column boxes of the rest output that hold columns
+  int T;           // rows per sequence: row m has RoPE position pos0 + m % T
+  int pos0;
+  const __nv_bfloat16* cos;  // [*, 128] rotary tables
+  const __nv_bfloat16* sin;
+  const float* bias;         // [n_tiles * 256], packed like the weight
+  int* err;
+};
+// Clusters of two CTAs that can be resident at once (0 on failure).
+int proj_gemm_max_clusters();
+// x / weight maps: 2-D, box {64, 128}; output maps: 2-D, box {64, 32}; all
+// 128-byte swizzled.  `clusters` persistent clusters of two CTAs.
+cudaError_t launch_proj_gemm(const CUtensorMap& xmap, const CUtensorMap& wmap,
+                             const CUtensorMap& qmap, const CUtensorMap& kmap,
+                             const CUtensorMap& vmap, const CUtensorMap& rmap,
+                             const ProjGemmArgs& a, int clusters, cudaStream_t stream);
+
 cudaError_t launch_gather_attention(const void* q, int64_t q_stride, const void* k,
                                     int64_t k_stride, const void* v, int64_t v_stride,
                                     const int32_t* indices, const uint8_t* mask, int k_sel,

@@ -301,6 +301,12 @@ class GatedSparseAttention(nn.Module):
 
         self._fused_weight: Optional[torch.Tensor] = None
         self._fused_bias: Optional[torch.Tensor] = None
+        # packed weight / bias of the projection GEMM with RoPE and the value
+        # gate in its epilogue (bf16, d_head 128); built on first use
+        self._packed: Optional[tuple] = None
+        # bf16 forwards take that fused projection when the sizes allow; False
+        # selects cuBLAS addmm + the separate RoPE/gate kernel
+        self.use_fused_epilogue = True
         self._stage_events: Optional[list] = None
         self._streams: dict = {}
         self._workspaces: dict = {}  # (device, stream, slot) -> indexer/top-k scratch
@@ -337,6 +343,7 @@ class GatedSparseAttention(nn.Module):
         b[o[7]:o[7] + hi] = self.indexer.idx_w_proj.bias.detach()
         self._fused_weight = w.contiguous()
         self._fused_bias = b.contiguous()
+        self._packed = None
 
     def _get_fused_weight(self):
         p = self.q_proj.weight
@@ -365,6 +372,49 @@ class GatedSparseAttention(nn.Module):
             "iq": proj[..., o[5]:o[5] + hi * di].unflatten(-1, (hi, di)),
             "ik": proj[..., o[6]:o[6] + di], "iw": proj[..., o[7]:o[7] + hi],
         }
+
+    def fused_epilogue_ok(self, dtype: torch.dtype) -> bool:
+        """Whether ``project_fused`` serves inputs of ``dtype``: bf16 modules with
+        128-channel heads and a hidden size that is a multiple of 256."""
+        return (self.use_fused_epilogue and dtype == torch.bfloat16
+                and self.q_proj.weight.dtype == torch.bfloat16 and self.d_head == 128
+                and self.hidden_size % 256 == 0)
+
+    def _get_packed(self):
+        p = self.q_proj.weight
+        if (self._packed is None or self._packed[0].device != p.device
+                or self._packed[0].dtype != p.dtype):
+            ix = self.indexer
+            self._packed = ops.fused_projection_pack(
+                {"q": self.q_proj.weight, "k": self.k_proj.weight, "v": self.v_proj.weight,
+                 "vg": self.value_gate.gate_proj.weight, "og": self.output_gate.gate_proj.weight,
+                 "iq": ix.idx_q_proj.weight, "ik": ix.idx_k_proj.weight,
+                 "iw": ix.idx_w_proj.weight, "vg_bias": self.value_gate.gate_proj.bias,
+                 "og_bias": self.output_gate.gate_proj.bias, "iw_bias": ix.idx_w_proj.bias},
+                ix.n_idx_heads, ix.d_indexer)
+        return self._packed
+
+    def project_fused(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                      pos0: int = 0, seq_len: Optional[int] = None, out: Optional[tuple] = None):
+        """Projection GEMM with RoPE and the value gate in its epilogue (one kernel).
+
+        Returns (q, k, v, parts): q, k, v [B, T, D] after RoPE / the value gate,
+        and ``parts`` the og / iq / ik / iw views of the rest columns.  Row t of
+        a sequence takes row pos0 + t of the rotary tables cos / sin."""
+        wp, bp = self._get_packed()
+        ix = self.indexer
+        q, k, v, rest = ops.fused_projection(x, wp, bp, self.num_heads, ix.n_idx_heads,
+                                             ix.d_indexer, cos, sin, pos0, seq_len, out)
+        return q, k, v, self.split_rest(rest)
+
+    def split_rest(self, rest: torch.Tensor) -> dict:
+        """og / iq / ik / iw views of a fused projection's rest columns."""
+        D = self.hidden_size
+        hi, di = self.indexer.n_idx_heads, self.indexer.d_indexer
+        o_iq, o_ik = D, D + hi * di
+        o_iw = o_ik + di
+        return {"og": rest[..., :D], "iq": rest[..., o_iq:o_ik].unflatten(-1, (hi, di)),
+                "ik": rest[..., o_ik:o_iw], "iw": rest[..., o_iw:o_iw + hi]}
 
     def select_rows(self, parts: dict, ik_all: torch.Tensor, q_pos0: int,
                     tkv: Optional[int] = None, bitmask_out: Optional[torch.Tensor] = None):
@@ -528,21 +578,31 @@ class GatedSparseAttention(nn.Module):
         B, T, D = x.shape
         x = x.contiguous()
         _nvtx_push("gsa_b200/forward")
-        with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
-            proj = self.project(x)
-        parts = self.split(proj)
         cos, sin = self.rotary_emb(T, x.device, x.dtype)
-        # Two streams, as the reference's pipeline (gsa_opt.py:654-711): the
-        # indexer + top-k (tensor/MUFU-bound) run beside RoPE + value gate
-        # (HBM-bound); the attention waits for both.
         main = torch.cuda.current_stream(x.device)
         side = self._side_stream(x.device) if side is None else side
-        side.wait_stream(main)
-        with torch.cuda.stream(side):
-            sel = self.select_blocks([(parts, parts["ik"], 0, T)], var_reduce, var_rows)[0]
-        with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
-            q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, self.num_heads,
-                                     v_src=parts["v"], vg_src=parts["vg"])
+        if self.fused_epilogue_ok(x.dtype):
+            # RoPE and the value gate run in the projection GEMM's epilogue; the
+            # indexer + top-k then run alone (gsa_opt.py:654-711 runs them beside
+            # the element-wise track_B work)
+            with _Stage(self, "k:proj_rope_gates", "gsa_b200/fused_proj_rope"):
+                q, k, v, parts = self.project_fused(x, cos, sin)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                sel = self.select_blocks([(parts, parts["ik"], 0, T)], var_reduce, var_rows)[0]
+        else:
+            with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
+                proj = self.project(x)
+            parts = self.split(proj)
+            # Two streams, as the reference's pipeline (gsa_opt.py:654-711): the
+            # indexer + top-k (tensor/MUFU-bound) run beside RoPE + value gate
+            # (HBM-bound); the attention waits for both.
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                sel = self.select_blocks([(parts, parts["ik"], 0, T)], var_reduce, var_rows)[0]
+            with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
+                q, k, v = ops.rope_gates(parts["q"], parts["k"], cos, sin, self.num_heads,
+                                         v_src=parts["v"], vg_src=parts["vg"])
         main.wait_stream(side)
         if isinstance(sel, tuple):  # index lists are new tensors; the bitmask is kept scratch
             for t in sel:
@@ -664,9 +724,19 @@ class GatedSparseAttention(nn.Module):
                 e = torch.cuda.Event()
                 e.record(h2d)
                 done_in.append(e)
-        w, bias = self._get_fused_weight()
+        fused = self.fused_epilogue_ok(x_host.dtype)
         cos, sin = self.rotary_emb(T, dev, x_host.dtype)
-        proj = torch.empty(1, T, self._proj_padded, device=dev, dtype=x_host.dtype)
+        if fused:  # RoPE and the value gate in the projection GEMM's epilogue
+            self._get_packed()
+            ix = self.indexer
+            proj = torch.empty(1, T, ops.fused_projection_rest_width(D, ix.n_idx_heads,
+                                                                     ix.d_indexer),
+                               device=dev, dtype=x_host.dtype)
+            parts_all = self.split_rest(proj)
+        else:
+            w, bias = self._get_fused_weight()
+            proj = torch.empty(1, T, self._proj_padded, device=dev, dtype=x_host.dtype)
+            parts_all = self.split(proj)
         q = torch.empty(1, T, D, device=dev, dtype=x_host.dtype)
         k = torch.empty_like(q)
         v = torch.empty_like(q)
@@ -678,7 +748,6 @@ class GatedSparseAttention(nn.Module):
         bm_flat = (torch.empty(sum(bm_sizes), device=dev, dtype=torch.int32) if bf16_tc
                    else None)
         bm_offs = [sum(bm_sizes[:i]) for i in range(len(bm_sizes))]
-        parts_all = self.split(proj)
         if keep is not None:
             keep.extend([x_dev, proj, q, k, v, attn, y, bm_flat])
         side.wait_stream(compute)  # the buffers above come from the current stream's pool
@@ -688,17 +757,24 @@ class GatedSparseAttention(nn.Module):
             r0, r1 = blocks[c]
             with torch.cuda.stream(side):
                 side.wait_event(done_in[c])
-                with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
-                    torch.addmm(bias, x_dev[0, r0:r1], w.t(), out=proj[0, r0:r1])
+                if fused:
+                    with _Stage(self, "k:proj_rope_gates", "gsa_b200/fused_proj_rope"):
+                        self.project_fused(x_dev[:, r0:r1], cos, sin, pos0=r0, seq_len=r1 - r0,
+                                           out=(q[:, r0:r1], k[:, r0:r1], v[:, r0:r1],
+                                                proj[:, r0:r1]))
+                else:
+                    with _Stage(self, "lib:proj_gemm", "gsa_b200/fused_proj"):
+                        torch.addmm(bias, x_dev[0, r0:r1], w.t(), out=proj[0, r0:r1])
                 rows = {name: t[:, r0:r1] for name, t in parts_all.items()}
                 bm_c = (bm_flat[bm_offs[c]:bm_offs[c] + bm_sizes[c]].view(
                     1, r1 - r0, ops.bitmask_words(r1)) if bf16_tc else None)
                 sel = self.select_rows(rows, parts_all["ik"][:, :r1], q_pos0=r0, tkv=r1,
                                        bitmask_out=bm_c)
-                with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
-                    ops.rope_gates(rows["q"], rows["k"], cos[r0:r1], sin[r0:r1], H,
-                                   v_src=rows["v"], vg_src=rows["vg"],
-                                   out=(q[:, r0:r1], k[:, r0:r1], v[:, r0:r1]))
+                if not fused:
+                    with _Stage(self, "k:rope_gates", "gsa_b200/rope_gates"):
+                        ops.rope_gates(rows["q"], rows["k"], cos[r0:r1], sin[r0:r1], H,
+                                       v_src=rows["v"], vg_src=rows["vg"],
+                                       out=(q[:, r0:r1], k[:, r0:r1], v[:, r0:r1]))
                 e = torch.cuda.Event()
                 e.record(side)
             return e, rows, sel
@@ -777,7 +853,7 @@ class GraphedForward:
             self.out = module._forward_impl(self.x, side=self._side)
         # the graph reads these by address: hold them even if the module later
         # replaces its caches (new sequence length, dtype, re-fused weights)
-        self._held = (module._fused_weight, module._fused_bias,
+        self._held = (module._fused_weight, module._fused_bias, module._packed,
                       getattr(module.indexer, "_bias32", None),
                       getattr(module.rotary_emb, "_tables", None), dict(module._workspaces))
 
@@ -833,7 +909,7 @@ class GraphedForwardHost:
         with torch.no_grad(), torch.cuda.graph(self.graph, stream=self._main):
             module._issue_host(self.x, self.out, chunks, device, *streams, keep=self._keep,
                                graphed=True)
-        self._held = (module._fused_weight, module._fused_bias,
+        self._held = (module._fused_weight, module._fused_bias, module._packed,
                       getattr(module.indexer, "_bias32", None),
                       getattr(module.rotary_emb, "_tables", None), dict(module._workspaces))
 

@@ -117,6 +117,77 @@ def rope_gates(q_src: torch.Tensor, k_src: torch.Tensor, cos: torch.Tensor, sin:
     return q, k, v
 
 
+def fused_projection_rows(hidden: int, n_idx_heads: int, d_indexer: int) -> int:
+    """Rows of the packed weight ``fused_projection`` takes (0: unsupported sizes)."""
+    return int(_lib.load().gsa_fused_projection_rows(hidden, n_idx_heads, d_indexer))
+
+
+def fused_projection_rest_width(hidden: int, n_idx_heads: int, d_indexer: int) -> int:
+    """Row width of the ``rest`` output (og | iq | ik | iw, padded to 64 columns)."""
+    return int(_lib.load().gsa_fused_projection_rest_width(hidden, n_idx_heads, d_indexer))
+
+
+def fused_projection_pack(weights: dict, n_idx_heads: int, d_indexer: int):
+    """Packed (weight [rows, D] bf16, bias [rows] fp32) for ``fused_projection``.
+
+    ``weights`` maps q, k, v, vg, og, iq, ik, iw to the nn.Linear weights and
+    vg_bias, og_bias, iw_bias to the biases (bf16, on one device)."""
+    w = {n: weights[n].detach().contiguous() for n in ("q", "k", "v", "vg", "og", "iq", "ik", "iw")}
+    b = {n: weights[n].detach().float().contiguous() for n in ("vg_bias", "og_bias", "iw_bias")}
+    _cuda(*w.values(), *b.values())
+    D = w["q"].shape[1]
+    if any(t.dtype != torch.bfloat16 for t in w.values()):
+        raise ValueError("fused_projection_pack takes bf16 weights")
+    rows = fused_projection_rows(D, n_idx_heads, d_indexer)
+    if rows == 0:
+        raise ValueError(f"unsupported sizes for the fused projection: D={D}")
+    wp = torch.empty(rows, D, device=w["q"].device, dtype=torch.bfloat16)
+    bp = torch.empty(rows, device=w["q"].device, dtype=torch.float32)
+    rc = _lib.load().gsa_fused_projection_pack(
+        *(w[n].data_ptr() for n in ("q", "k", "v", "vg", "og", "iq", "ik", "iw")),
+        *(b[n].data_ptr() for n in ("vg_bias", "og_bias", "iw_bias")),
+        D, n_idx_heads, d_indexer, wp.data_ptr(), bp.data_ptr(), _stream())
+    _lib.check(rc, "gsa_fused_projection_pack")
+    return wp, bp
+
+
+def fused_projection(x: torch.Tensor, w_packed: torch.Tensor, b_packed: torch.Tensor,
+                     num_heads: int, n_idx_heads: int, d_indexer: int, cos: torch.Tensor,
+                     sin: torch.Tensor, pos0: int = 0, seq_len: int | None = None,
+                     out: tuple | None = None):
+    """Projection GEMM with RoPE and the value gate in its epilogue (bf16).
+
+    x [B, T, D] (unit inner stride); cos / sin [rows, 128] bf16 tables; row t of
+    a sequence takes table row pos0 + t (``seq_len`` = rows per sequence,
+    default T).  Returns (q, k, v, rest): q, k, v [B, T, D] contiguous (RoPE'd,
+    gated) and rest [B, T, rest width] = og | iq | ik | iw | padding.  ``out``
+    = (q, k, v, rest) supplies them."""
+    _cuda(x, w_packed, b_packed, cos, sin)
+    B, T, D = x.shape
+    M = B * T
+    if x.dtype != torch.bfloat16 or w_packed.dtype != torch.bfloat16:
+        raise ValueError("fused_projection is bf16")
+    xs = _rows(x, D, "x")
+    if B > 1 and x.stride(0) != T * xs:
+        raise ValueError("x must have uniform row strides across the batch")
+    rw = fused_projection_rest_width(D, n_idx_heads, d_indexer)
+    if out is None:
+        q = torch.empty(B, T, D, device=x.device, dtype=x.dtype)
+        k, v = torch.empty_like(q), torch.empty_like(q)
+        rest = torch.empty(B, T, rw, device=x.device, dtype=x.dtype)
+    else:
+        q, k, v, rest = out
+    cos = cos.to(torch.bfloat16).contiguous()
+    sin = sin.to(torch.bfloat16).contiguous()
+    rc = _lib.load().gsa_fused_projection(
+        x.data_ptr(), xs, w_packed.data_ptr(), b_packed.data_ptr(), M, D, num_heads,
+        D // num_heads, n_idx_heads, d_indexer, T if seq_len is None else seq_len, pos0,
+        cos.data_ptr(), sin.data_ptr(), cos.shape[0], q.data_ptr(), k.data_ptr(), v.data_ptr(),
+        rest.data_ptr(), rest.stride(-2), _stream())
+    _lib.check(rc, "gsa_fused_projection")
+    return q, k, v, rest
+
+
 def apply_rotary_pos_emb(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
     """Reference-compatible RoPE: q, k [B, T, H, d]; cos, sin broadcastable to [1, T, 1, d]."""
     B, T, H, d = q.shape

@@ -222,8 +222,16 @@ class ShardedGSA:
 
     def _forward_rows(self, x_loc: torch.Tensor, gather: bool = True) -> torch.Tensor:
         m = self.model
-        with _Stage(m, "lib:proj_gemm", "gsa_b200/fused_proj"):
-            proj = m.project(x_loc)
+        if m.fused_epilogue_ok(x_loc.dtype):
+            # RoPE and the value gate in the projection's epilogue, with the
+            # rotary table rows of this rank's positions
+            cos, sin = m.rotary_emb(self.T, x_loc.device, x_loc.dtype)
+            pos = self._positions(x_loc.device)
+            with _Stage(m, "k:proj_rope_gates", "gsa_b200/fused_proj_rope"):
+                proj = m.project_fused(x_loc, cos.index_select(0, pos), sin.index_select(0, pos))
+        else:
+            with _Stage(m, "lib:proj_gemm", "gsa_b200/fused_proj"):
+                proj = m.project(x_loc)
         if not gather:
             outs = self._rows_from_projection(proj, x_loc.dtype)
             with _Stage(m, "lib:o_proj", "gsa_b200/o_proj"):
@@ -241,28 +249,33 @@ class ShardedGSA:
         with _Stage(m, "comm:out_allgather_wait", "gsa_b200/out_allgather"):
             return gat.finish()
 
-    def _rows_from_projection(self, proj: torch.Tensor, dtype, per_block=None) -> list:
+    def _rows_from_projection(self, proj, dtype, per_block=None) -> list:
         """Everything after the projection GEMM of this rank's rows: gathers,
-        RoPE + value gate, selection and attention.  Returns the gated attention
-        output of each block ([1, n, D], in the order of ``self.blocks``); with
-        ``per_block(i, o, n, attn)`` that callback receives each block as soon as
-        it is computed."""
+        RoPE + value gate (unless ``proj`` is the (q, k, v, parts) of
+        ``project_fused``, which ran them in its epilogue), selection and
+        attention.  Returns the gated attention output of each block ([1, n, D],
+        in the order of ``self.blocks``); with ``per_block(i, o, n, attn)`` that
+        callback receives each block as soon as it is computed."""
         m = self.model
         T, H = self.T, m.num_heads
-        dev = proj.device
+        fused = isinstance(proj, tuple)
+        parts = proj[3] if fused else m.split(proj)
+        dev = parts["ik"].device
         order = self._row_order(dev)
-        parts = m.split(proj)
         # the selection needs only the indexer keys of the whole sequence (2 MB at
         # T=16K): gathered while RoPE runs
         ik_loc = parts["ik"][0]
         g_ik = torch.empty((self.world, *ik_loc.shape), dtype=ik_loc.dtype, device=dev)
         w_ik = all_gather_async(g_ik, ik_loc, self.group)
-        cos, sin = m.rotary_emb(T, dev, dtype)
-        pos = self._positions(dev)
-        with _Stage(m, "k:rope_gates", "gsa_b200/rope_gates"):
-            q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
-                                     sin.index_select(0, pos), H, v_src=parts["v"],
-                                     vg_src=parts["vg"])
+        if fused:
+            q, k, v = proj[:3]
+        else:
+            cos, sin = m.rotary_emb(T, dev, dtype)
+            pos = self._positions(dev)
+            with _Stage(m, "k:rope_gates", "gsa_b200/rope_gates"):
+                q, k, v = ops.rope_gates(parts["q"], parts["k"], cos.index_select(0, pos),
+                                         sin.index_select(0, pos), H, v_src=parts["v"],
+                                         vg_src=parts["vg"])
         # keys and values of the whole sequence: gathered while the blocks select
         gk = torch.empty((self.world, *k.shape[1:]), dtype=k.dtype, device=dev)
         gv = torch.empty_like(gk)
@@ -340,11 +353,27 @@ class ShardedGSA:
                 ev.record(h2d)
             arrived.append((ev, off, e - s))
             off += e - s
-        w, bias = m._get_fused_weight()
-        proj = torch.empty(1, Tl, m._proj_padded, device=dev, dtype=x_local_host.dtype)
-        for ev, o, n in arrived:
-            compute.wait_event(ev)
-            torch.addmm(bias, x_dev[0, o:o + n], w.t(), out=proj[0, o:o + n])
+        if m.fused_epilogue_ok(x_local_host.dtype):
+            # each block's rows hold the consecutive positions s..e-1
+            ix = m.indexer
+            rest = torch.empty(1, Tl, ops.fused_projection_rest_width(D, ix.n_idx_heads,
+                                                                      ix.d_indexer),
+                               device=dev, dtype=x_local_host.dtype)
+            q = torch.empty(1, Tl, D, device=dev, dtype=x_local_host.dtype)
+            k, v = torch.empty_like(q), torch.empty_like(q)
+            cos, sin = m.rotary_emb(self.T, dev, x_local_host.dtype)
+            for (ev, o, n), (s, _) in zip(arrived, self.blocks):
+                compute.wait_event(ev)
+                m.project_fused(x_dev[:, o:o + n], cos, sin, pos0=s, seq_len=n,
+                                out=(q[:, o:o + n], k[:, o:o + n], v[:, o:o + n],
+                                     rest[:, o:o + n]))
+            proj = (q, k, v, m.split_rest(rest))
+        else:
+            w, bias = m._get_fused_weight()
+            proj = torch.empty(1, Tl, m._proj_padded, device=dev, dtype=x_local_host.dtype)
+            for ev, o, n in arrived:
+                compute.wait_event(ev)
+                torch.addmm(bias, x_dev[0, o:o + n], w.t(), out=proj[0, o:o + n])
         y = torch.empty(1, Tl, D, device=dev, dtype=x_local_host.dtype)
 
         def block_out(i, o, n, a):

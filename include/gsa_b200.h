@@ -351,6 +351,59 @@ GSA_API int gsa_output_gate(const void* o, int64_t o_stride,
                     void* out, int64_t out_stride,
                     int dtype, int rows, int width, void* stream);
 
+/*
+ * Fused projection GEMM with RoPE and the value gate in its epilogue (bf16).
+ * Replaces the mega-GEMM of gsa_opt.py:582-609 (torch.addmm over the
+ * concatenated weights, biases added) together with the element-wise track_B
+ * work after it (gsa_opt.py:683-696: value gate, RoPE on q and k):
+ *
+ *   q_out = RoPE(x Wq^T), k_out = RoPE(x Wk^T)          [M, D] contiguous
+ *   v_out = (x Wv^T) * sigmoid(x Wvg^T + b_vg)            [M, D] contiguous
+ *   rest  = og | iq | ik | iw = x [Wog; Wiq; Wik; Wiw]^T + [b_og; 0; 0; b_iw]
+ *           [M, rest_stride], columns [0, D + H_I*d_I + d_I + H_I) written
+ *
+ * rounded to bf16 where the unfused torch ops round (each projection once,
+ * then as gsa_rope_gates).  Row m (of M = B*T) has the rotary position
+ * pos0 + m % T, i.e. row pos0 + m % T of the [table_rows, d] bf16 tables
+ * cos / sin.  The weights come packed by gsa_fused_projection_pack:
+ * w_packed [gsa_fused_projection_rows(D, H_I, d_I), D] bf16 and b_packed
+ * float32 of the same row count.  Requires d == 128, D = H*d a multiple of
+ * 256, 16-byte aligned rows, rest_stride >= gsa_fused_projection_rest_width.
+ * One launch of a persistent tcgen05 kernel (clusters of two CTAs); the
+ * accumulation order differs from cuBLAS's, so single outputs may differ from
+ * the unfused path by one bf16 rounding step.  Allocates nothing.
+ */
+GSA_API int gsa_fused_projection(const void* x, int64_t x_stride,
+                         const void* w_packed, const float* b_packed,
+                         int M, int D, int H, int d, int H_I, int d_I,
+                         int T, int pos0, const void* cos, const void* sin,
+                         int64_t table_rows,
+                         void* q_out, void* k_out, void* v_out,
+                         void* rest, int64_t rest_stride, void* stream);
+
+/* Rows of the packed weight (256 per column tile), 0 for unsupported sizes. */
+GSA_API int64_t gsa_fused_projection_rows(int D, int H_I, int d_I);
+
+/* Minimum rest_stride: D + H_I*d_I + d_I + H_I rounded up to 64. */
+GSA_API int64_t gsa_fused_projection_rest_width(int D, int H_I, int d_I);
+
+/*
+ * Packs the module's projection weights for gsa_fused_projection (device
+ * copies on `stream`; call again after the weights change).  Replaces
+ * fuse_projections (gsa_opt.py:582-609) for this layout:
+ *   w_q, w_k, w_v, w_vg, w_og [D, D]; w_iq [H_I*d_I, D]; w_ik [d_I, D];
+ *   w_iw [H_I, D]: bf16, contiguous (nn.Linear.weight layout);
+ *   b_vg, b_og [D], b_iw [H_I]: float32 (NULL = zero).
+ * Output: w_packed [rows, D] bf16 and b_packed [rows] float32, rows =
+ * gsa_fused_projection_rows(D, H_I, d_I).
+ */
+GSA_API int gsa_fused_projection_pack(const void* w_q, const void* w_k,
+                         const void* w_v, const void* w_vg, const void* w_og,
+                         const void* w_iq, const void* w_ik, const void* w_iw,
+                         const float* b_vg, const float* b_og, const float* b_iw,
+                         int D, int H_I, int d_I,
+                         void* w_packed, float* b_packed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

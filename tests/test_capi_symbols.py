@@ -76,3 +76,24 @@ def test_adaptive_k_entry_points_on_the_host(lib):
     rc = lib.gsa_row_variance(None, 8, 1, 1, 8, 0, None, None, None)
     assert rc == 1
 
+
+
+def test_fused_projection_layout_queries(lib):
+    # hidden 2048, 4 indexer heads of 64: q 8 + k 8 + v/vg 16 + rest 10 column tiles
+    # of 256 rows; rest columns og 2048 | iq 256 | ik 64 | iw 4 = 2372 -> 2432
+    assert lib.gsa_fused_projection_rows(2048, 4, 64) == 42 * 256
+    assert lib.gsa_fused_projection_rest_width(2048, 4, 64) == 2432
+    assert lib.gsa_fused_projection_rows(512, 4, 64) == (2 + 2 + 4 + 4) * 256
+    # hidden sizes that are not a multiple of 256 are not served
+    assert lib.gsa_fused_projection_rows(640, 4, 64) == 0
+    assert lib.gsa_fused_projection_rest_width(640, 4, 64) == 0
+    # host-side checks before any device work: d != 128 is unsupported (3),
+    # negative sizes are invalid (1), no rows is a no-op
+    rc = lib.gsa_fused_projection(None, 0, None, None, 4, 512, 8, 64, 4, 64, 4, 0, None, None,
+                                  0, None, None, None, None, 0, None)
+    assert rc == 3 and b"d == 128" in lib.gsa_last_error_string()
+    rc = lib.gsa_fused_projection(None, 0, None, None, -1, 512, 4, 128, 4, 64, 4, 0, None, None,
+                                  0, None, None, None, None, 0, None)
+    assert rc == 1
+    assert lib.gsa_fused_projection(None, 0, None, None, 0, 512, 4, 128, 4, 64, 4, 0, None, None,
+                                    0, None, None, None, None, 0, None) == 0
