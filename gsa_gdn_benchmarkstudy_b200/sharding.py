@@ -74,50 +74,32 @@ def all_gather_async(out: torch.Tensor, t: torch.Tensor, group):
 
 class RowBlockGather:
     """The full [1, T, W] output from every rank's two zig-zag row blocks,
-    gathered piece by piece so that each all-gather overlaps the work that
-    follows it.
+    gathered one block at a time so that a block's all-gather overlaps the
+    work that follows it.
 
     Rank r's first block is sequence block r, so the ranks' first blocks
-    gathered rank-major are sequence blocks 0..P-1 and land in place.  Rank r's
-    second block is sequence block 2P-1-r; it is gathered in ``chunks`` equal
-    row pieces (the last piece's gather is the only one nothing follows, so
-    smaller pieces leave less of it exposed), which arrive rank-major and in
-    reverse block order and are copied into place once they have all arrived."""
+    gathered rank-major are sequence blocks 0..P-1 and land in place; rank r's
+    second block is sequence block 2P-1-r, so the second gather comes in
+    reverse order and is copied into place once it has arrived."""
 
-    def __init__(self, T: int, world: int, width: int, dtype, device, chunks: int = 1):
+    def __init__(self, T: int, world: int, width: int, dtype, device):
         self.world, self.n = world, T // (2 * world)
-        if chunks < 1 or self.n % chunks:
-            raise ValueError(f"{chunks} chunks do not divide a block of {self.n} rows")
-        self.chunks = chunks
         self.out = torch.empty(1, T, width, dtype=dtype, device=device)
-        # piece c of every rank's second block: [chunks, P, n / chunks, W]
-        self.late = torch.empty(chunks, world, self.n // chunks, width, dtype=dtype,
-                                device=device)
+        self.late = torch.empty(world, self.n, width, dtype=dtype, device=device)
         self.works = []
 
-    def add(self, i: int, block: torch.Tensor, group, chunk: int = 0) -> None:
-        """Start gathering this rank's block ``i`` (0 or 1), [n, W]; for block 1
-        piece ``chunk`` of it, [n / chunks, W]."""
+    def add(self, i: int, block: torch.Tensor, group) -> None:
+        """Start gathering this rank's block ``i`` (0 or 1), [n, W]."""
         P, n = self.world, self.n
-        target = self.out[0, :P * n].view(P, n, -1) if i == 0 else self.late[chunk]
+        target = self.out[0, :P * n].view(P, n, -1) if i == 0 else self.late
         self.works.append(all_gather_async(target, block, group))
 
     def finish(self) -> torch.Tensor:
         for w in self.works:
             w.wait()
         P, n = self.world, self.n
-        second = self.late.permute(1, 0, 2, 3).reshape(P, n, -1)  # rank r's second block
-        self.out[0, P * n:].copy_(second.flip(0).reshape(P * n, -1))
+        self.out[0, P * n:].copy_(self.late.flip(0).reshape(P * n, -1))
         return self.out
-
-
-def late_block_chunks(n: int) -> int:
-    """Pieces the last row block is attended and gathered in: up to 4, each a
-    whole number of 128-row attention tiles and at least 256 rows."""
-    for c in (4, 2):
-        if n % (128 * c) == 0 and n // c >= 256:
-            return c
-    return 1
 
 
 def zigzag_order(T: int, world: int, device) -> torch.Tensor:
@@ -256,13 +238,12 @@ class ShardedGSA:
                 return F.linear(torch.cat(outs, dim=1), m.o_proj.weight)
         # o_proj and the output all-gather per block: the first (early, light)
         # block's gather runs while the second block computes
-        gat = RowBlockGather(self.T, self.world, m.hidden_size, x_loc.dtype, x_loc.device,
-                             late_block_chunks(self.T // (2 * self.world)))
+        gat = RowBlockGather(self.T, self.world, m.hidden_size, x_loc.dtype, x_loc.device)
 
-        def block_out(i, c, o, n, a):
+        def block_out(i, o, n, a):
             with _Stage(m, "lib:o_proj", "gsa_b200/o_proj"):
                 y = F.linear(a[0], m.o_proj.weight)
-            gat.add(i, y, self.kv_group, c)
+            gat.add(i, y, self.kv_group)
 
         self._rows_from_projection(proj, x_loc.dtype, per_block=block_out)
         with _Stage(m, "comm:out_allgather_wait", "gsa_b200/out_allgather"):
@@ -273,10 +254,8 @@ class ShardedGSA:
         RoPE + value gate (unless ``proj`` is the (q, k, v, parts) of
         ``project_fused``, which ran them in its epilogue), selection and
         attention.  Returns the gated attention output of each block ([1, n, D],
-        in the order of ``self.blocks``; the last block in ``late_block_chunks``
-        row pieces); with ``per_block(i, c, o, n, attn)`` that callback receives
-        each piece (block i, piece c, local rows [o, o + n)) as soon as it is
-        computed."""
+        in the order of ``self.blocks``); with ``per_block(i, o, n, attn)`` that
+        callback receives each block as soon as it is computed."""
         m = self.model
         T, H = self.T, m.num_heads
         fused = isinstance(proj, tuple)
@@ -287,10 +266,7 @@ class ShardedGSA:
         # T=16K): gathered while RoPE runs
         ik_loc = parts["ik"][0]
         g_ik = torch.empty((self.world, *ik_loc.shape), dtype=ik_loc.dtype, device=dev)
-        # on the K/V group, ahead of the K/V gathers: one communicator runs its
-        # collectives in order, so the small k_I gather the selection waits for
-        # does not share the links with them
-        w_ik = all_gather_async(g_ik, ik_loc, self.kv_group)
+        w_ik = all_gather_async(g_ik, ik_loc, self.group)
         if fused:
             q, k, v = proj[:3]
         else:
@@ -335,19 +311,11 @@ class ShardedGSA:
             k_full = unshard_rows(gk, order)
             v_full = unshard_rows(gv, order)
         outs = []
-        late_chunks = late_block_chunks(blocks[-1][4])
         for i, ((pb, s, e, o, n), sel) in enumerate(zip(blocks, sels)):
-            nc = late_chunks if i == len(blocks) - 1 else 1
-            for c in range(nc):
-                c0, c1 = n * c // nc, n * (c + 1) // nc
-                pbc = {key: t[:, c0:c1] for key, t in pb.items()}
-                selc = (tuple(t[:, c0:c1] for t in sel) if isinstance(sel, tuple)
-                        else sel[:, c0:c1])
-                a = m.attend_selected(pbc, selc, k_full[:, :s + c1], v_full[:, :s + c1],
-                                      q[:, o + c0:o + c1], q_pos0=s + c0)
-                if per_block is not None:
-                    per_block(i, c, o + c0, c1 - c0, a)
-                outs.append(a)
+            a = m.attend_selected(pb, sel, k_full[:, :e], v_full[:, :e], q[:, o:o + n], q_pos0=s)
+            if per_block is not None:
+                per_block(i, o, n, a)
+            outs.append(a)
         return outs
 
     def forward_host(self, x_local_host: torch.Tensor) -> torch.Tensor:
@@ -408,7 +376,7 @@ class ShardedGSA:
                 torch.addmm(bias, x_dev[0, o:o + n], w.t(), out=proj[0, o:o + n])
         y = torch.empty(1, Tl, D, device=dev, dtype=x_local_host.dtype)
 
-        def block_out(i, c, o, n, a):
+        def block_out(i, o, n, a):
             torch.mm(a[0], m.o_proj.weight.t(), out=y[0, o:o + n])
             d2h.wait_stream(compute)
             with torch.cuda.stream(d2h):

@@ -9,8 +9,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from gsa_gdn_benchmarkstudy_b200.sharding import (RowBlockGather, causal_row_cost, gather_batch,
-                                                  gather_rows, late_block_chunks, unshard_rows,
-                                                  zigzag_blocks, zigzag_order)
+                                                  gather_rows, unshard_rows, zigzag_blocks,
+                                                  zigzag_order)
 
 
 @pytest.mark.parametrize("T,world", [(16384, 1), (16384, 2), (16384, 8), (65536, 8), (64, 4)])
@@ -66,33 +66,17 @@ def _worker(rank, world, port, T, q):
         local = torch.cat([full[:, s:e] for s, e in zigzag_blocks(T, world, rank)], dim=1)
         got = gather_rows(local, T, dist.group.WORLD)
         ok_rows = torch.equal(got, full)
-        # the per-block form the sharded forward uses: block 0 gathered first,
-        # then the second block whole or in equal row pieces
-        (s0, e0), (s1, e1) = zigzag_blocks(T, world, rank)
-        for chunks in (1, 2, 5):
-            gat = RowBlockGather(T, world, 3, torch.float32, torch.device("cpu"), chunks)
-            gat.add(0, full[0, s0:e0], dist.group.WORLD)
-            m = (e1 - s1) // chunks
-            for c in range(chunks):
-                gat.add(1, full[0, s1 + c * m:s1 + (c + 1) * m], dist.group.WORLD, c)
-            ok_rows = ok_rows and torch.equal(gat.finish(), full)
+        # the per-block form the sharded forward uses: block 0 gathered first
+        gat = RowBlockGather(T, world, 3, torch.float32, torch.device("cpu"))
+        for i, (s, e) in enumerate(zigzag_blocks(T, world, rank)):
+            gat.add(i, full[0, s:e], dist.group.WORLD)
+        ok_rows = ok_rows and torch.equal(gat.finish(), full)
         xb = torch.arange(4 * 5 * 2, dtype=torch.float32).view(4, 5, 2)
         per = 4 // world
         gb = gather_batch(xb[rank * per:(rank + 1) * per], dist.group.WORLD)
         q.put((rank, ok_rows, torch.equal(gb, xb)))
     finally:
         dist.destroy_process_group()
-
-
-def test_late_block_chunks():
-    # whole 128-row attention tiles, at least 256 rows a piece, at most 4 pieces
-    assert late_block_chunks(4096) == 4  # T=16384 on 2 GPUs
-    assert late_block_chunks(1024) == 4  # T=16384 on 8 GPUs
-    assert late_block_chunks(512) == 2
-    assert late_block_chunks(256) == 1
-    assert late_block_chunks(1000) == 1
-    with pytest.raises(ValueError):
-        RowBlockGather(40, 2, 3, torch.float32, torch.device("cpu"), 3)  # 10 rows in 3 pieces
 
 
 def test_gloo_world2_reassembles_row_and_batch_shards():
