@@ -253,8 +253,11 @@ __device__ __forceinline__ void bits_to_lists(Sh& sh, int nwords, int32_t* irow,
 // k of one row in adaptive mode (gsa_explained.ipynb, "Adaptive Top-K" cell):
 //   avg_var = mean over the batch's rows of row_var, clamped to >= 1e-6
 //   k = clamp(floor(k_base * avg_var / max(row_var, 1e-6)), k_min, k_max)
-// in fp32 with round-to-nearest multiply and divide, as torch computes it.
-// A NaN row variance gives k_max.
+// The mean is the double-precision sum of the row variances over the row
+// count, rounded once to fp32 (torch's fp32 mean can differ from it in the
+// last ulp, and then a row whose ratio lies that close to an integer gets a k
+// one apart); the rest is fp32 with round-to-nearest multiply and divide, as
+// torch computes it.  A NaN row variance gives k_max.
 __device__ __forceinline__ int adaptive_row_k(const AdaptiveK& ad, int64_t row) {
   const float avg =
       fmaxf(static_cast<float>(*ad.var_sum / static_cast<double>(ad.var_rows)), 1e-6f);
