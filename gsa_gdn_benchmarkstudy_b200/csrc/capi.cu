@@ -128,6 +128,28 @@ int make_map_bf16_3d(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
   return GSA_OK;
 }
 
+// 3-D fp32 map of indexer score rows: [B][Tq][nkeys] with row stride
+// `row_bytes`; box {16, 32, 1} with 64-byte swizzle (the layout the indexer
+// epilogue stages), stores clipped past the last row and key.
+int make_map_scores(CUtensorMap* map, float* base, uint64_t nkeys, uint64_t Tq, uint64_t B,
+                    uint64_t row_bytes) {
+  PFN_encodeTiled_t fn = encode_fn();
+  if (!fn) return set_error(GSA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {nkeys, Tq, B};
+  const cuuint64_t strides[2] = {row_bytes, row_bytes * Tq};
+  const cuuint32_t box[3] = {16, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled failed (%d)",
+                  static_cast<int>(r));
+    return GSA_ERR_CUDA;
+  }
+  return GSA_OK;
+}
+
 // 2-D bf16 map over [rows][cols] with row stride `row_bytes`; box {64,
 // box_rows} with 128-byte swizzle; loads fill zeros out of bounds, stores
 // are clipped there.
@@ -237,10 +259,13 @@ int indexer_impl(const void* q, int64_t q_stride, const void* k, int64_t k_strid
     CUtensorMap qmap, kmap;
     rc = make_tk_maps(&qmap, &kmap, q, q_stride, k, k_stride, B, Tq, Tkv, 1, 0);
     if (rc) return rc;
+    CUtensorMap omap;
+    rc = make_map_scores(&omap, out, Tkv, Tq, B, out_stride * 4);
+    if (rc) return rc;
     gsa::IndexerTkArgs a = tk_args(w, w_stride, bias, scale, B, Tq, Tkv, q_pos0, st->err);
     a.out = out;
     a.out_stride = out_stride;
-    return finish(gsa::launch_indexer_tk(gsa::kIdxStore, qmap, kmap, a, s));
+    return finish(gsa::launch_indexer_tk(gsa::kIdxStore, qmap, kmap, omap, a, s));
   }
   if (H_I > 8 || d_I > 128 || H_I * d_I > 512)
     return set_error(GSA_ERR_UNSUPPORTED, "indexer heads/dims beyond the CUDA-core kernel");
@@ -337,7 +362,10 @@ int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k
   a1.key_off = off;
   a1.out = ws;
   a1.out_stride = stride;
-  cudaError_t e = gsa::launch_indexer_tk(gsa::kIdxSample, qmap_s, kmap_s, a1, s);
+  CUtensorMap omap_s;
+  rc = make_map_scores(&omap_s, ws, a1.nkeys, Tq, B, stride * 4);
+  if (rc) return rc;
+  cudaError_t e = gsa::launch_indexer_tk(gsa::kIdxSample, qmap_s, kmap_s, omap_s, a1, s);
   if (e != cudaSuccess) return set_cuda_error(e);
   // 2. per-row brackets [lo, hi] of the k-th score
   e = gsa::launch_select_threshold(ws, stride, B, Tq, Tkv, q_pos0, step, off, k_sel, kSampleZ,
@@ -350,7 +378,7 @@ int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k
   a3.bitmask_words = sel_words;
   a3.cand_off = cand_off;
   a3.cand_per_list = per_list;
-  e = gsa::launch_indexer_tk(gsa::kIdxSelect, qmap, kmap, a3, s);
+  e = gsa::launch_indexer_tk(gsa::kIdxSelect, qmap, kmap, omap_s, a3, s);
   if (e != cudaSuccess) return set_cuda_error(e);
   // 4. full score rows of the rows whose bracket missed
   e = gsa::launch_select_scan(stats, B, Tq, Tkv, q_pos0, k_sel, gsa::indexer_tk_rows_per_cta(), s);
@@ -358,7 +386,7 @@ int indexer_topk_fused(const void* q, int64_t q_stride, const void* k, int64_t k
   gsa::IndexerTkArgs a4 = a;
   a4.out = ws;
   a4.out_stride = stride;
-  e = gsa::launch_indexer_tk(gsa::kIdxStoreFailed, qmap, kmap, a4, s);
+  e = gsa::launch_indexer_tk(gsa::kIdxStoreFailed, qmap, kmap, omap_s, a4, s);
   if (e != cudaSuccess) return set_cuda_error(e);
   // 5. exact completion of every row
   return finish(gsa::launch_select_fixup(reinterpret_cast<const uint32_t*>(ws), stride, sel_words,

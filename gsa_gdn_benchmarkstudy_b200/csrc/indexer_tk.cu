@@ -76,10 +76,33 @@ struct IdxSmem {
 };
 constexpr int kIdxCtlBytes = 256;
 static_assert(sizeof(IdxSmem) <= kIdxCtlBytes, "control block exceeds its slot");
+// kStore / kSample write their scores with TMA: each epilogue warp stages
+// its 32 rows x 16 keys of a sub-tile (fp32, 64-byte rows, 64B swizzle) and
+// stores the box in one bulk copy, so a row's keys reach L2 as whole
+// sectors instead of 16 bytes per row per warp store instruction.
+template <int kMode>
+constexpr bool idx_tma_store() { return kMode == kIdxStore || kMode == kIdxSample; }
+constexpr int kIdxBoxBytes = 32 * 16 * 4;  // one warp's staging box
+template <int kMode>
+constexpr int idx_staging_bytes() { return idx_tma_store<kMode>() ? kIdxEpiWarps * kIdxBoxBytes : 0; }
 template <int kMode>
 constexpr int idx_smem_bytes() {
-  return 1024 /*align slack*/ + kIdxHeads * kIdxQBytes + kIdxStages * kIdxKBytes + kIdxCtlBytes +
+  return 1024 /*align slack*/ + kIdxHeads * kIdxQBytes + kIdxStages * kIdxKBytes +
+         idx_staging_bytes<kMode>() + kIdxCtlBytes +
          (kMode == kIdxSelect ? kIdxBM * kIdxBitsPitch * 4 : 0);
+}
+
+// Byte offset of 16-byte chunk c (0..3) of row r in a box of 64-byte rows
+// with the TMA 64-byte swizzle (chunk index XOR bits 1-2 of the row).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t c) {
+  return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int x, int y, int z,
+                                             const void* smem_src) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem_src))
+               : "memory");
 }
 
 __device__ __forceinline__ void epi_bar() {
@@ -89,13 +112,15 @@ __device__ __forceinline__ void epi_bar() {
 template <int kMode>
 __global__ void __launch_bounds__(kIdxThreads, 2)
     indexer_tk_kernel(const __grid_constant__ CUtensorMap qmap,
-                      const __grid_constant__ CUtensorMap kmap, IndexerTkArgs a) {
+                      const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap omap, IndexerTkArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* q_s = smem;                                   // 4 x 16 KB
   uint8_t* k_s = smem + kIdxHeads * kIdxQBytes;          // 4 x 4 KB
-  IdxSmem* sh = reinterpret_cast<IdxSmem*>(k_s + kIdxStages * kIdxKBytes);
+  uint8_t* staging = k_s + kIdxStages * kIdxKBytes;       // 1024-byte aligned
+  IdxSmem* sh = reinterpret_cast<IdxSmem*>(staging + idx_staging_bytes<kMode>());
   uint32_t* bits_s = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(sh) + kIdxCtlBytes);
 
   const int tid = threadIdx.x;
@@ -304,13 +329,37 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
             ncand = a.cand_per_list + 1;  // overflow: the row takes the exact fallback
           }
         }
-      } else if (store_row) {
-        if constexpr (kMode == kIdxStore || kMode == kIdxStoreFailed) {
+      } else if constexpr (idx_tma_store<kMode>()) {
+        if constexpr (kMode == kIdxStore) {
 #pragma unroll
           for (int e = 0; e < kCols; ++e)
             if (j0 + e >= jlim) acc[e] = -INFINITY;
         }
-        // kSample: samples past the row's last key are never read
+        // this warp's box: rows (its lanes) x keys [j0, j0 + 16); TMA clips
+        // rows past Tq and keys past the launch's last key
+        uint8_t* box = staging + warp * kIdxBoxBytes;
+        if (s > 0 && lane == 0)  // the previous store has read the box
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
+        const uint32_t bx = smem_u32(box);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(bx + sw64_offset(lane, c)),
+                       "f"(acc[4 * c]), "f"(acc[4 * c + 1]), "f"(acc[4 * c + 2]),
+                       "f"(acc[4 * c + 3])
+                       : "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&omap, j0, row0 + (warp & 3) * 32, b, box);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      } else if (store_row) {
+        if constexpr (kMode == kIdxStoreFailed) {
+#pragma unroll
+          for (int e = 0; e < kCols; ++e)
+            if (j0 + e >= jlim) acc[e] = -INFINITY;
+        }
         if (j0 + kCols <= a.nkeys) {
           float4* dst = reinterpret_cast<float4*>(orow + j0);
 #pragma unroll
@@ -324,6 +373,11 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
       }
     }
 
+    if constexpr (idx_tma_store<kMode>()) {
+      // the stores of this warp are complete before its shared memory goes
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      __syncwarp();
+    }
     if constexpr (kMode == kIdxSelect) {
       // ---- flush: the tile's bitmask words, then each row's counters
       epi_bar();
@@ -357,7 +411,8 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
 }
 
 template <int kMode>
-cudaError_t launch_mode(const CUtensorMap& qmap, const CUtensorMap& kmap, const IndexerTkArgs& a,
+cudaError_t launch_mode(const CUtensorMap& qmap, const CUtensorMap& kmap,
+                        const CUtensorMap& omap, const IndexerTkArgs& a,
                         cudaStream_t stream) {
   // once per device; two threads racing here both set the same attribute
   static std::atomic<bool> attr_set[kMaxDevices];
@@ -374,7 +429,7 @@ cudaError_t launch_mode(const CUtensorMap& qmap, const CUtensorMap& kmap, const 
   const int n_kc = (a.nkeys + idx_chunk<kMode>() - 1) / idx_chunk<kMode>();
   if (n_qt > 65535 || a.B > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid(n_kc, n_qt, a.B);
-  indexer_tk_kernel<kMode><<<grid, kIdxThreads, smem, stream>>>(qmap, kmap, a);
+  indexer_tk_kernel<kMode><<<grid, kIdxThreads, smem, stream>>>(qmap, kmap, omap, a);
   return cudaGetLastError();
 }
 
@@ -385,13 +440,14 @@ int indexer_tk_keys_per_tile() { return kIdxBN; }
 int indexer_tk_keys_per_cta() { return kIdxChunk; }
 
 cudaError_t launch_indexer_tk(int mode, const CUtensorMap& qmap, const CUtensorMap& kmap,
+                              const CUtensorMap& omap,
                               const IndexerTkArgs& a, cudaStream_t stream) {
   if (a.B == 0 || a.Tq == 0 || a.nkeys == 0) return cudaSuccess;
   switch (mode) {
-    case kIdxStore: return launch_mode<kIdxStore>(qmap, kmap, a, stream);
-    case kIdxSample: return launch_mode<kIdxSample>(qmap, kmap, a, stream);
-    case kIdxSelect: return launch_mode<kIdxSelect>(qmap, kmap, a, stream);
-    case kIdxStoreFailed: return launch_mode<kIdxStoreFailed>(qmap, kmap, a, stream);
+    case kIdxStore: return launch_mode<kIdxStore>(qmap, kmap, omap, a, stream);
+    case kIdxSample: return launch_mode<kIdxSample>(qmap, kmap, omap, a, stream);
+    case kIdxSelect: return launch_mode<kIdxSelect>(qmap, kmap, omap, a, stream);
+    case kIdxStoreFailed: return launch_mode<kIdxStoreFailed>(qmap, kmap, omap, a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -75,13 +75,16 @@ struct IndexerTkArgs {
   int k_sel;               // kStoreFailed: k of the failure test
   int* err;
 };
-// Tensor maps: q box {64, indexer_tk_rows_per_cta()}, k box {64, indexer_tk_keys_per_tile()}.
+// Tensor maps: q box {64, indexer_tk_rows_per_cta()}, k box {64, indexer_tk_keys_per_tile()};
+// omap (kStore, kSample) is the fp32 score map {nkeys, Tq, B} with box {16, 32, 1} and
+// 64-byte swizzle, unused by the other modes.
 // A CTA covers indexer_tk_keys_per_cta() launch keys: two candidate lists.
 int indexer_tk_rows_per_cta();
 int indexer_tk_keys_per_tile();
 int indexer_tk_keys_per_cta();
 cudaError_t launch_indexer_tk(int mode, const CUtensorMap& qmap, const CUtensorMap& kmap,
-                              const IndexerTkArgs& a, cudaStream_t stream);
+                              const CUtensorMap& omap, const IndexerTkArgs& a,
+                              cudaStream_t stream);
 
 // Per row: from the row's sampled scores (samples[row * stride + i], i < the
 // row's causal sample count, sample i = key i*key_step + key_off) estimate the
