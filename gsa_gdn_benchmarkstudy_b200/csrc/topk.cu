@@ -131,11 +131,28 @@ struct PosBins {
   }
 };
 
+// Per-instance shared-memory sizes.  The short-range instance (key range <
+// kLongKeyRange, rows of at most kLongKeyRange / 32 bitmask words) keeps 512
+// candidates: its smaller footprint (16.5 against 24.7 KB) leaves more of the
+// SM's L1 to the rows' second read at the same 8 CTAs per SM (registers
+// bound those).  Measured at T=16K: top-k 0.255 -> 0.235 ms, indexer + top-k
+// 0.472 -> 0.441 ms; a lower register cap for more CTAs per SM (10, 11 or 12)
+// and a larger L1 carve-out at fewer CTAs were slower.  The long instance
+// keeps kCandCap.
+constexpr int kShortCandCap = 512;
+template <int kGroups>
+constexpr int topk_words() { return kGroups == kEmitLong ? kMaxWords : kLongKeyRange / 32; }
+template <int kGroups>
+constexpr int topk_cand_cap() { return kGroups == kEmitLong ? kCandCap : kShortCandCap; }
+
+template <int kWords, int kCap>
 struct alignas(16) TopkShared {
+  static constexpr int kNumWords = kWords;
+  static constexpr int kNumCand = kCap;
   int hist[kBins];
-  uint32_t cand_key[kCandCap];
-  int cand_idx[kCandCap];
-  uint32_t bits[kMaxWords];
+  uint32_t cand_key[kCap];
+  int cand_idx[kCap];
+  uint32_t bits[kWords];
   int warp_a[kTopkWarps];
   int warp_b[kTopkWarps];
   uint32_t red_min[kTopkWarps];
@@ -272,8 +289,8 @@ __device__ __forceinline__ int adaptive_row_k(const AdaptiveK& ad, int64_t row) 
 // Selection of one row (the whole CTA): the k_sel best of the row's n valid
 // scores srow[0, n) into irow / mrow (k_width slots; NULL = not wanted) and
 // brow (bm_words words; NULL = not wanted).
-template <bool kFinite, int kGroups>
-__device__ __forceinline__ void topk_row(TopkShared& sh, const float* __restrict__ srow, int n,
+template <bool kFinite, int kGroups, typename Sh>
+__device__ __forceinline__ void topk_row(Sh& sh, const float* __restrict__ srow, int n,
                                          int Tkv, int k_sel, int k_width, int32_t* irow,
                                          uint8_t* mrow, uint32_t* brow, int64_t bm_words) {
   const int tid = threadIdx.x;
@@ -311,7 +328,7 @@ __device__ __forceinline__ void topk_row(TopkShared& sh, const float* __restrict
 
   // =================================================================== fast path
   bool done = false;
-  if (n > k_sel && nwords <= kMaxWords) {
+  if (n > k_sel && nwords <= Sh::kNumWords) {
     // 1. sample range
     uint32_t smin = 0xFFFFFFFFu, smax = 0u;
     int sfin = 0;
@@ -388,7 +405,7 @@ __device__ __forceinline__ void topk_row(TopkShared& sh, const float* __restrict
         const int bstar = sh.sh_digit;
         const int krem = k_sel - sh.sh_above;
         const int bcount = sh.sh_bin;
-        if (bcount > kCandCap) return false;
+        if (bcount > Sh::kNumCand) return false;
         bins.set_threshold(bstar);
         // 4. bits for higher bins, candidates of the threshold bin; G 32-key groups per
         // step, whose loads are in flight together
@@ -573,7 +590,7 @@ __device__ __forceinline__ void topk_row(TopkShared& sh, const float* __restrict
         break;
       }
       // compact the class into the candidate list once it is short enough
-      if (!use_cand && bin_count <= kCandCap) {
+      if (!use_cand && bin_count <= Sh::kNumCand) {
         if (tid == 0) sh.n_cand = 0;
         __syncthreads();
         for (int j = tid; j < n; j += kTopkThreads) {
@@ -671,7 +688,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     const float* __restrict__ scores, int64_t score_stride, int Tq, int Tkv, int q_pos0,
     int k_fixed, int k_width, AdaptiveK ad, int32_t* __restrict__ indices,
     uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask, int64_t bm_words) {
-  __shared__ TopkShared sh;
+  __shared__ TopkShared<topk_words<kGroups>(), topk_cand_cap<kGroups>()> sh;
   const int64_t row = blockIdx.x;  // b * Tq + r
   const int r = static_cast<int>(row % Tq);
   const int n = min(q_pos0 + r + 1, Tkv);
@@ -1094,7 +1111,7 @@ __global__ void __launch_bounds__(kTopkThreads) select_fallback_kernel(
     const float* __restrict__ ws, int64_t ws_stride, const SelectRowStats* __restrict__ stats,
     int64_t rows, int Tq, int Tkv, int q_pos0, int k_sel, int32_t* __restrict__ indices,
     uint8_t* __restrict__ mask, uint32_t* __restrict__ bitmask, int64_t bm_words) {
-  __shared__ TopkShared sh;
+  __shared__ TopkShared<topk_words<kGroups>(), topk_cand_cap<kGroups>()> sh;
   __shared__ int64_t failed[kTopkThreads];
   __shared__ int nfailed;
   // the CTA's rows, kTopkThreads at a time: each thread checks one, the failed
