@@ -439,11 +439,30 @@ __device__ __forceinline__ void topk_row(Sh& sh, const float* __restrict__ srow,
           // threshold-bin keys (a few per row) collected only in steps that have one
           const int hi_m1 = bins.hi_m1, lo_edge = bins.lo_edge;
           full_end = s0 + max(0, min(s1, n) - s0) / (G * 32) * (G * 32);
-          for (int jb = s0; jb < full_end; jb += G * 32) {
-            const float* p = srow + jb + lane;
-            int x[G];
+          // Short steps issue the next step's loads before this step's ballots
+          // (T=16K: top-k 0.223 -> 0.214 ms; two steps ahead measured the same).
+          // Long steps load in place: their 16 groups already keep the loads
+          // in flight, and a second set would cost registers (64 -> 79).
+          constexpr bool kPrefetch = G != kEmitLong;
+          int xn[G];
+          if (kPrefetch && s0 < full_end) {
 #pragma unroll
-            for (int g = 0; g < G; ++g) x[g] = __float_as_int(__ldg(p + g * 32));
+            for (int g = 0; g < G; ++g) xn[g] = __float_as_int(__ldg(srow + s0 + lane + g * 32));
+          }
+          for (int jb = s0; jb < full_end; jb += G * 32) {
+            int x[G];
+            if constexpr (kPrefetch) {
+#pragma unroll
+              for (int g = 0; g < G; ++g) x[g] = xn[g];
+              if (jb + G * 32 < full_end) {
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                  xn[g] = __float_as_int(__ldg(srow + jb + G * 32 + lane + g * 32));
+              }
+            } else {
+#pragma unroll
+              for (int g = 0; g < G; ++g) x[g] = __float_as_int(__ldg(srow + jb + lane + g * 32));
+            }
             uint32_t w[G];
             bool in = false;
 #pragma unroll
