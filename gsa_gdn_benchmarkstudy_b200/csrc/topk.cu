@@ -192,9 +192,11 @@ __device__ __forceinline__ void block_minmax_count(Sh& sh, uint32_t& kmin, uint3
 }
 
 // Suffix scan over sh.hist (bins counted from the top down): finds the bin
-// holding the krem-th largest key; sets sh_digit / sh_above / sh_bin.
+// holding the krem-th largest key; sets sh_digit / sh_above / sh_bin (left
+// unset when the histogram holds fewer than krem keys).  Returns the
+// histogram's total count, in every thread.
 template <int kNB = kBins, typename Sh>
-__device__ __forceinline__ void find_threshold_bin(Sh& sh, int krem) {
+__device__ __forceinline__ int find_threshold_bin(Sh& sh, int krem) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kBpt = kNB / kTopkThreads;
   int own[kBpt], loc = 0;
@@ -213,6 +215,9 @@ __device__ __forceinline__ void find_threshold_bin(Sh& sh, int krem) {
   __syncthreads();
   int before = inc - loc;
   for (int w = 0; w < warp; ++w) before += sh.warp_a[w];
+  int total = 0;
+#pragma unroll
+  for (int w = 0; w < kTopkWarps; ++w) total += sh.warp_a[w];
   if (before < krem && before + loc >= krem) {
     int cum = before;
 #pragma unroll
@@ -226,6 +231,7 @@ __device__ __forceinline__ void find_threshold_bin(Sh& sh, int krem) {
     }
   }
   __syncthreads();
+  return total;
 }
 
 // Ascending column list (irow) and mask 1 (mrow) of the set bits of
@@ -329,6 +335,24 @@ __device__ __forceinline__ void topk_row(Sh& sh, const float* __restrict__ srow,
   // =================================================================== fast path
   bool done = false;
   if (n > k_sel && nwords <= Sh::kNumWords) {
+    // float4 loads per thread in flight in the histogram pass: 8 when the rows
+    // come from L2 (key range under 32K: 0.276 -> 0.268 ms at T=16K), 4 when
+    // they come from DRAM (8 cost 12% at T=64K).  Rows without -inf (kFinite)
+    // issue the first batch here, beside the sample loads, so that its latency
+    // overlaps the range reduction (T=16K: indexer + top-k 0.417 -> 0.413 ms,
+    // T=8K x 8: 0.891 -> 0.877 ms); elsewhere the batch held across the
+    // reduction cost registers (56 -> 72) and time.
+    constexpr int U = kGroups == kEmitLong ? 4 : 8;
+    const float4* s4 = reinterpret_cast<const float4*>(srow);
+    const int nv = vec_ok ? n >> 2 : 0;
+    float4 f0[U];
+    if constexpr (kFinite) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = u * kTopkThreads + tid;
+        f0[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
     // 1. sample range
     uint32_t smin = 0xFFFFFFFFu, smax = 0u;
     int sfin = 0;
@@ -363,45 +387,38 @@ __device__ __forceinline__ void topk_row(Sh& sh, const float* __restrict__ srow,
           const int bn = bins.hist_bin(f, inc);
           atomicAdd(&sh.hist[bn], inc);
         };
-        int jv = 0;
-        if (vec_ok) {
-          const float4* s4 = reinterpret_cast<const float4*>(srow);
-          const int nv = n >> 2;
-          // float4 loads per thread in flight: 8 when the rows come from L2 (key
-          // range under 32K: 0.276 -> 0.268 ms at T=16K), 4 when they come from
-          // DRAM (8 cost 12% at T=64K)
-          constexpr int U = kGroups == kEmitLong ? 4 : 8;
-          for (int v0 = 0; v0 < nv; v0 += U * kTopkThreads) {
-            float4 f[U];
+        auto hist_batch = [&](const float4 (&f)[U], int v0) {
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-              const int v = v0 + u * kTopkThreads + tid;
-              f[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-              if (v0 + u * kTopkThreads + tid < nv) {
-                hist_key(f[u].x);
-                hist_key(f[u].y);
-                hist_key(f[u].z);
-                hist_key(f[u].w);
-              }
+          for (int u = 0; u < U; ++u) {
+            if (v0 + u * kTopkThreads + tid < nv) {
+              hist_key(f[u].x);
+              hist_key(f[u].y);
+              hist_key(f[u].z);
+              hist_key(f[u].w);
             }
           }
-          jv = nv << 2;
+        };
+        int v_first = 0;
+        if constexpr (kFinite) {
+          hist_batch(f0, 0);
+          v_first = U * kTopkThreads;
         }
+        for (int v0 = v_first; v0 < nv; v0 += U * kTopkThreads) {
+          float4 f[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int v = v0 + u * kTopkThreads + tid;
+            f[u] = v < nv ? __ldg(s4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          hist_batch(f, v0);
+        }
+        const int jv = nv << 2;
         for (int j = jv + tid; j < n; j += kTopkThreads) hist_key(__ldg(srow + j));
         __syncthreads();
         // finite keys = histogram total
-        constexpr int kBpt = kBins / kTopkThreads;
-        int nfin = 0;
-#pragma unroll
-        for (int q = 0; q < kBpt; ++q) nfin += sh.hist[tid * kBpt + q];
-        uint32_t d0 = 0, d1 = 0;
-        block_minmax_count(sh, d0, d1, nfin);
+        // 3. threshold bin; the scan also counts the finite keys
+        const int nfin = find_threshold_bin(sh, k_sel);
         if (nfin <= k_sel) return false;
-        // 3. threshold bin
-        find_threshold_bin(sh, k_sel);
         const int bstar = sh.sh_digit;
         const int krem = k_sel - sh.sh_above;
         const int bcount = sh.sh_bin;
