@@ -382,7 +382,28 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
 
     // epilogue: merge the two parities, O / l (+ output gate), bf16 store of
-    // this warp's 64 output channels (par * 64 ..)
+    // this warp's 64 output channels (par * 64 ..).  The gates bf16(sigmoid(og))
+    // are loaded and computed first, so that their latency overlaps the merge
+    // and the wait for the last P.V.
+    const uint32_t col0 = par * 64;
+    const __nv_bfloat16* grow_p =
+        (a.og && row_ok)
+            ? static_cast<const __nv_bfloat16*>(a.og) + grow * a.og_stride + h * kAtD + col0
+            : nullptr;
+    uint32_t gates[32];  // bf16x2: channels (2e, 2e+1)
+    if (grow_p) {
+      uint4 graw[8];
+#pragma unroll
+      for (int qd = 0; qd < 8; ++qd) graw[qd] = reinterpret_cast<const uint4*>(grow_p)[qd];
+#pragma unroll
+      for (int qd = 0; qd < 8; ++qd) {
+        const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&graw[qd]);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2)
+          gates[qd * 4 + (e >> 1)] = pack_bf16x2(sigmoid_ref(__bfloat162float(ge[e])),
+                                                 sigmoid_ref(__bfloat162float(ge[e + 1])));
+      }
+    }
     sh->xm[par][i] = m;
     sh->xl[par][i] = l;
     asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
@@ -396,12 +417,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     if (ok) {
       tc_fence_after();
       const float inv_l = lsum > 0.f ? 1.0f / lsum : 0.f;
-      const uint32_t col0 = par * 64;
       __nv_bfloat16* orow =
           static_cast<__nv_bfloat16*>(a.out) + grow * a.out_stride + h * kAtD + col0;
-      const __nv_bfloat16* grow_p =
-          a.og ? static_cast<const __nv_bfloat16*>(a.og) + grow * a.og_stride + h * kAtD + col0
-               : nullptr;
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         uint32_t oe[32], oo[32];
@@ -418,20 +435,14 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         const uint32_t* ov = oe;
         uint32_t packed[16];
         if (grow_p) {
-          const uint4* gp = reinterpret_cast<const uint4*>(grow_p + cc * 32);
 #pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            const uint4 gv = gp[qd];
-            const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
-#pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              const int idx = qd * 8 + e;
-              const float o0 = bf16_round(__uint_as_float(ov[idx]));
-              const float o1 = bf16_round(__uint_as_float(ov[idx + 1]));
-              const float g0 = bf16_round(sigmoid_ref(__bfloat162float(ge[e])));
-              const float g1 = bf16_round(sigmoid_ref(__bfloat162float(ge[e + 1])));
-              packed[idx >> 1] = pack_bf16x2(o0 * g0, o1 * g1);
-            }
+          for (int e = 0; e < 32; e += 2) {
+            const uint32_t g = gates[cc * 16 + (e >> 1)];
+            const float o0 = bf16_round(__uint_as_float(ov[e]));
+            const float o1 = bf16_round(__uint_as_float(ov[e + 1]));
+            const float g0 = __uint_as_float(g << 16);
+            const float g1 = __uint_as_float(g & 0xFFFF0000u);
+            packed[e >> 1] = pack_bf16x2(o0 * g0, o1 * g1);
           }
         } else {
 #pragma unroll
