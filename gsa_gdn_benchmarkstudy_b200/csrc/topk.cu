@@ -531,10 +531,26 @@ __device__ __forceinline__ void topk_row(Sh& sh, const float* __restrict__ srow,
         for (int c = tid; c < nc; c += kTopkThreads) {
           const uint32_t u = sh.cand_key[c];
           const int ji = sh.cand_idx[c];
+          // four candidates' loads in flight per step, compares without branches
+          // (T=16K: indexer + top-k 0.413 -> 0.407 ms)
           int rank = 0;
-          for (int o = 0; o < nc; ++o) {
+          int o = 0;
+          for (; o + 4 <= nc; o += 4) {
+            uint32_t uo[4];
+            int io[4];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uo[q4] = sh.cand_key[o + q4];
+              io[q4] = sh.cand_idx[o + q4];
+            }
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              rank += ((uo[q4] > u) | ((uo[q4] == u) & (io[q4] < ji))) ? 1 : 0;
+          }
+          for (; o < nc; ++o) {
             const uint32_t uo = sh.cand_key[o];
-            rank += (uo > u || (uo == u && sh.cand_idx[o] < ji)) ? 1 : 0;
+            const int io = sh.cand_idx[o];
+            rank += ((uo > u) | ((uo == u) & (io < ji))) ? 1 : 0;
           }
           if (rank < krem) atomicOr(&sh.bits[ji >> 5], 1u << (ji & 31));
         }
