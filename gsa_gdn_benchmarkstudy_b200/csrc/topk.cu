@@ -29,6 +29,7 @@
 // which the row's min and max keys differ, with candidate compaction, and a
 // warp-segmented emit.  Both paths implement the same selection rule.
 #include <algorithm>
+#include <cstddef>
 #include <type_traits>
 
 #include "kernels.h"
@@ -199,11 +200,23 @@ template <int kNB = kBins, typename Sh>
 __device__ __forceinline__ int find_threshold_bin(Sh& sh, int krem) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kBpt = kNB / kTopkThreads;
+  static_assert(kBpt % 4 == 0 && offsetof(Sh, hist) % 16 == 0, "16-byte histogram reads");
+  // this thread's bins kNB-1-kBpt*tid down to kNB-kBpt*(tid+1): one contiguous
+  // block, read as 16-byte vectors (scalar reads at a stride of kBpt words
+  // would conflict kBpt/2-fold across the warp)
   int own[kBpt], loc = 0;
+  {
+    const int4* blk = reinterpret_cast<const int4*>(sh.hist + kNB - kBpt * (tid + 1));
 #pragma unroll
-  for (int q = 0; q < kBpt; ++q) {
-    own[q] = sh.hist[kNB - 1 - (kBpt * tid + q)];
-    loc += own[q];
+    for (int v = 0; v < kBpt / 4; ++v) {
+      const int4 x = blk[v];
+      own[kBpt - 1 - 4 * v] = x.x;
+      own[kBpt - 2 - 4 * v] = x.y;
+      own[kBpt - 3 - 4 * v] = x.z;
+      own[kBpt - 4 - 4 * v] = x.w;
+    }
+#pragma unroll
+    for (int q = 0; q < kBpt; ++q) loc += own[q];
   }
   int inc = loc;
 #pragma unroll
@@ -367,7 +380,8 @@ __device__ __forceinline__ void topk_row(Sh& sh, const float* __restrict__ srow,
         sfin = 1;
       }
     }
-    for (int b = tid; b < kBins; b += kTopkThreads) sh.hist[b] = 0;
+    for (int b = tid; b < kBins / 4; b += kTopkThreads)
+      reinterpret_cast<int4*>(sh.hist)[b] = make_int4(0, 0, 0, 0);
     for (int w = tid; w < nwords; w += kTopkThreads) sh.bits[w] = 0u;
     if (tid == 0) sh.n_cand = 0;
     block_minmax_count(sh, smin, smax, sfin);
